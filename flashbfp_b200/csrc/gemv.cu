@@ -1,0 +1,426 @@
+// gemv.cu — fused OABF dequant-GEMV for decode (1 <= M <= 16 tokens) on sm_100a.
+//
+// Replaces oabf_gemm_kernel (flash_bfp/triton_kernel.py:22-86) for small M together with
+// the outlier SpMV and bias of OABFLinear.forward (triton_kernel.py:339-362):
+//     y[m, n] = sum_k x[m, k] * W_full[n, k] + bias[n]       (fp32 accumulation)
+//
+// Weights stream straight from the packed reference layout (11 bytes per 16 weights) and
+// are dequantised in registers into bf16 tensor-core operands:
+//   * a lane owns a whole 16-element block of its two rows (g, g+8) for four consecutive
+//     mma.m16n8k16 steps (the k-slots of a step belong to four different blocks — the dot
+//     product does not care, and the activation fragment is permuted to match), so the
+//     per-block work (sign spread, exponent) is paid once per 16 weights;
+//   * a weight pair (elements q, q+4 of nibble word w) becomes the bf16 pair
+//     +-(128 + m) * 2^e by bit operations only: mantissa nibble into bits 0-3, exponent
+//     field (e + 134) into bits 7-14, sign into bit 15. A second MMA with the pair
+//     -+128 * 2^e (same signs/exponent, no nibble) against the same activations cancels
+//     the 128 offset inside the tensor core, leaving sum(s * m * 2^e * x); the 1/15 of the
+//     format is applied once in the epilogue;
+//   * the activation chunk is staged in shared memory permuted into fragment order, with a
+//     negated copy for the cancelling MMA, 16-byte pieces XOR-swizzled by k-block.
+// Work split: a CTA of 8 warps covers 64 rows x one 64-block (1024-column) chunk of K; each
+// warp takes a 16-row tile and half of the chunk. Partial sums of the chunks meet in an fp32
+// workspace via red.global.add; the last warp to arrive at a row tile (arrival counter)
+// adds bias, converts, stores y and returns the workspace and counter to zero.
+// Outliers are pre-grouped by (row tile, chunk) (fbfp_outlier_tiles_build) and handled by
+// the two warps of that tile/chunk with shared-memory float atomics.
+#include "common.cuh"
+#include "scan.cuh"
+
+namespace fbfp {
+
+constexpr int kGemvWarps = 8;
+constexpr int kGemvThreads = kGemvWarps * 32;
+constexpr int kRowsPerCta = 64;        // 4 row tiles of 16
+constexpr int kHalfKb = 32;            // k-blocks per warp (half a chunk)
+
+struct GemvArgs {
+  const void* x;
+  int x_dtype, m;
+  int64_t ldx;
+  const int8_t* ex;
+  const uint16_t* sg;
+  const uint2* pay;
+  int64_t n_out, k_in, kb_row, npad;
+  const uint32_t* entries;
+  const int32_t* seg_ptr;
+  const void* bias;
+  int bias_dtype;
+  void* y;
+  int y_dtype;
+  int64_t ldy;
+  float* ws;           // [m][npad] fp32 partial sums
+  int32_t* counters;   // [ceil(npad/16)] arrivals per row tile
+  int n_chunks;
+};
+
+__device__ __forceinline__ void mma_bf16_16816(float (&d)[4], uint32_t a0, uint32_t a1,
+                                               uint32_t a2, uint32_t a3, uint32_t b0,
+                                               uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 "
+      "{%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};\n"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+__device__ __forceinline__ uint32_t ld_nc_u16(const uint16_t* p) {
+  unsigned short v;
+  asm volatile("ld.global.nc.u16 %0, [%1];\n" : "=h"(v) : "l"(p));
+  return v;
+}
+__device__ __forceinline__ int ld_nc_s8(const int8_t* p) {
+  short v;
+  asm volatile("ld.global.nc.s8 %0, [%1];\n" : "=h"(v) : "l"(p));
+  return v;
+}
+__device__ __forceinline__ uint2 ld_nc_u64(const uint2* p) {
+  uint2 v;
+  asm volatile("ld.global.nc.v2.u32 {%0,%1}, [%2];\n" : "=r"(v.x), "=r"(v.y) : "l"(p));
+  return v;
+}
+__device__ __forceinline__ void red_add_f32(float* p, float v) {
+  asm volatile("red.global.add.f32 [%0], %1;\n" ::"l"(p), "f"(v) : "memory");
+}
+
+// Activation element position inside the staged chunk: element el (0..15) of k-block kbl,
+// token tok. Piece 0 holds pairs (0,4)(1,5)(2,6)(3,7), piece 1 pairs (8,12)..(11,15),
+// pieces 2/3 the negated copies; piece p of (kbl, tok) sits at slot p ^ (kbl & 3).
+__device__ __forceinline__ int x_piece_slot(int kbl, int tok, int m, int piece) {
+  return ((kbl * m + tok) << 2) + (piece ^ (kbl & 3));
+}
+
+template <int NT>
+__global__ void __launch_bounds__(kGemvThreads)
+gemv_kernel(const GemvArgs a) {
+  extern __shared__ uint4 xs[];                            // [64 kb][m][4] pieces
+  __shared__ float s_out[kGemvWarps][16][16];              // outlier partials [row][token]
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int g = lane >> 2, t = lane & 3;
+  const int m = a.m;
+  const int chunk = blockIdx.y;
+  const int64_t kb_c0 = (int64_t)chunk * kChunkKb;
+  const int64_t kb_c1 = min(kb_c0 + kChunkKb, a.kb_row);
+  const int nkb = (int)(kb_c1 - kb_c0);
+
+  // ---- stage the activation chunk (bf16, permuted, with negated copy) ----
+  for (int idx = threadIdx.x; idx < nkb * m; idx += kGemvThreads) {
+    const int kbl = idx / m, tok = idx - kbl * m;
+    const int64_t k0 = (kb_c0 + kbl) * kBlock;
+    uint32_t h[16];
+    if (a.x_dtype == FBFP_BF16) {
+      const uint16_t* xr = reinterpret_cast<const uint16_t*>(a.x) + tok * a.ldx + k0;
+      if (k0 + 16 <= a.k_in && ((uintptr_t)xr & 15) == 0) {
+        const uint4 q0 = reinterpret_cast<const uint4*>(xr)[0];
+        const uint4 q1 = reinterpret_cast<const uint4*>(xr)[1];
+        const uint32_t u[8] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w};
+#pragma unroll
+        for (int j = 0; j < 8; ++j) { h[2 * j] = u[j] & 0xFFFF; h[2 * j + 1] = u[j] >> 16; }
+      } else {
+#pragma unroll
+        for (int j = 0; j < 16; ++j) h[j] = (k0 + j < a.k_in) ? xr[j] : 0u;
+      }
+    } else {
+#pragma unroll
+      for (int j = 0; j < 16; ++j)
+        h[j] = (k0 + j < a.k_in) ? float_to_bf16_bits(load_as_float(a.x, a.x_dtype, tok * a.ldx + k0 + j)) : 0u;
+    }
+    uint4 p0, p1;
+    p0.x = h[0] | (h[4] << 16);  p0.y = h[1] | (h[5] << 16);
+    p0.z = h[2] | (h[6] << 16);  p0.w = h[3] | (h[7] << 16);
+    p1.x = h[8] | (h[12] << 16); p1.y = h[9] | (h[13] << 16);
+    p1.z = h[10] | (h[14] << 16); p1.w = h[11] | (h[15] << 16);
+    const uint32_t NEG = 0x80008000u;
+    const uint4 n0 = make_uint4(p0.x ^ NEG, p0.y ^ NEG, p0.z ^ NEG, p0.w ^ NEG);
+    const uint4 n1 = make_uint4(p1.x ^ NEG, p1.y ^ NEG, p1.z ^ NEG, p1.w ^ NEG);
+    xs[x_piece_slot(kbl, tok, m, 0)] = p0;
+    xs[x_piece_slot(kbl, tok, m, 1)] = p1;
+    xs[x_piece_slot(kbl, tok, m, 2)] = n0;
+    xs[x_piece_slot(kbl, tok, m, 3)] = n1;
+  }
+  for (int i = lane; i < 256; i += 32) (&s_out[warp][0][0])[i] = 0.f;
+  __syncthreads();
+
+  const int64_t rt = (int64_t)blockIdx.x * 4 + (warp & 3);
+  if (rt * 16 >= a.npad) return;                          // row tile past the matrix
+  const int half = warp >> 2;
+  const int64_t row0 = rt * 16 + g, row1 = row0 + 8;
+  const bool rv0 = row0 < a.npad, rv1 = row1 < a.npad;
+  const int64_t kb_lo = kb_c0 + half * kHalfKb;
+  const int64_t kb_hi = min(kb_lo + kHalfKb, kb_c1);
+
+  float acc[NT][4];
+#pragma unroll
+  for (int n = 0; n < NT; ++n) acc[n][0] = acc[n][1] = acc[n][2] = acc[n][3] = 0.f;
+
+  const int64_t base0 = row0 * a.kb_row, base1 = row1 * a.kb_row;
+  for (int64_t kb4 = kb_lo; kb4 < kb_hi; kb4 += 4) {
+    const int64_t kb = kb4 + t;
+    const bool ok = kb < kb_hi;
+    const bool ok0 = ok && rv0, ok1 = ok && rv1;
+    const uint2 p0 = ok0 ? ld_nc_u64(a.pay + base0 + kb) : make_uint2(0u, 0u);
+    const uint2 p1 = ok1 ? ld_nc_u64(a.pay + base1 + kb) : make_uint2(0u, 0u);
+    const uint32_t s0 = ok0 ? ld_nc_u16(a.sg + base0 + kb) : 0u;
+    const uint32_t s1 = ok1 ? ld_nc_u16(a.sg + base1 + kb) : 0u;
+    const int e0 = ok0 ? ld_nc_s8(a.ex + base0 + kb) : 0;
+    const int e1 = ok1 ? ld_nc_s8(a.ex + base1 + kb) : 0;
+    // bf16 exponent field of 128 * 2^e in both halves (zero for an absent block)
+    const uint32_t K0 = ok0 ? (uint32_t)(e0 + 134) * 0x00800080u : 0u;
+    const uint32_t K1 = ok1 ? (uint32_t)(e1 + 134) * 0x00800080u : 0u;
+    // sign bit j at j and j + 12: pair (q, q+4) lands on bits 15/31 after << (15 - q),
+    // pair (q+8, q+12) after << (7 - q)
+    const uint32_t y0 = s0 | (s0 << 12), y1 = s1 | (s1 << 12);
+
+    uint32_t xv[NT][8], xn[NT][8];
+    const int kbl = (int)(kb - kb_c0);
+#pragma unroll
+    for (int n = 0; n < NT; ++n) {
+      const int tok = n * 8 + g;
+      if (ok && tok < m) {
+        const uint4 q0 = xs[x_piece_slot(kbl, tok, m, 0)];
+        const uint4 q1 = xs[x_piece_slot(kbl, tok, m, 1)];
+        const uint4 q2 = xs[x_piece_slot(kbl, tok, m, 2)];
+        const uint4 q3 = xs[x_piece_slot(kbl, tok, m, 3)];
+        xv[n][0] = q0.x; xv[n][1] = q0.y; xv[n][2] = q0.z; xv[n][3] = q0.w;
+        xv[n][4] = q1.x; xv[n][5] = q1.y; xv[n][6] = q1.z; xv[n][7] = q1.w;
+        xn[n][0] = q2.x; xn[n][1] = q2.y; xn[n][2] = q2.z; xn[n][3] = q2.w;
+        xn[n][4] = q3.x; xn[n][5] = q3.y; xn[n][6] = q3.z; xn[n][7] = q3.w;
+      } else {
+#pragma unroll
+        for (int j = 0; j < 8; ++j) { xv[n][j] = 0u; xn[n][j] = 0u; }
+      }
+    }
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      const uint32_t SM = 0x80008000u, NM = 0x000F000Fu;
+      const uint32_t cA0 = ((y0 << (15 - q)) & SM) | K0;   // row g,   elements q, q+4
+      const uint32_t cB0 = ((y0 << (7 - q)) & SM) | K0;    // row g,   elements q+8, q+12
+      const uint32_t cA1 = ((y1 << (15 - q)) & SM) | K1;   // row g+8
+      const uint32_t cB1 = ((y1 << (7 - q)) & SM) | K1;
+      const uint32_t vA0 = ((p0.x >> (4 * q)) & NM) | cA0;
+      const uint32_t vB0 = ((p0.y >> (4 * q)) & NM) | cB0;
+      const uint32_t vA1 = ((p1.x >> (4 * q)) & NM) | cA1;
+      const uint32_t vB1 = ((p1.y >> (4 * q)) & NM) | cB1;
+#pragma unroll
+      for (int n = 0; n < NT; ++n) {
+        mma_bf16_16816(acc[n], vA0, vA1, vB0, vB1, xv[n][q], xv[n][4 + q]);
+        mma_bf16_16816(acc[n], cA0, cA1, cB0, cB1, xn[n][q], xn[n][4 + q]);
+      }
+    }
+  }
+
+  // ---- outliers of this (row tile, chunk), split between the two half-warps ----
+  if (a.entries) {
+    const int seg = (int)(rt * a.n_chunks + chunk);
+    const int lo = a.seg_ptr[seg], hi = a.seg_ptr[seg + 1];
+    const uint16_t* xh = reinterpret_cast<const uint16_t*>(xs);
+    for (int i = lo + half * 32 + lane; i < hi; i += 64) {
+      const uint32_t e = __ldg(a.entries + i);
+      const float v = __half2float(__ushort_as_half((unsigned short)(e & 0xFFFF)));
+      const int col = (e >> 16) & 0x3FF, r = (e >> 26) & 0xF;
+      const int kbl = col >> 4, el = col & 15;
+      const int piece = el >> 3, e7 = el & 7;
+      const int pos = ((e7 & 3) << 1) + (e7 >> 2);
+      for (int tok = 0; tok < m; ++tok) {
+        const float xv = bf16_bits_to_float(xh[x_piece_slot(kbl, tok, m, piece) * 8 + pos]);
+        atomicAdd(&s_out[warp][r][tok], v * xv);
+      }
+    }
+    __syncwarp();
+  }
+
+  // ---- fold into the fp32 workspace ----
+  const float inv15 = 1.0f / 15.0f;
+#pragma unroll
+  for (int n = 0; n < NT; ++n) {
+    const int tk0 = n * 8 + 2 * t, tk1 = tk0 + 1;
+    if (rv0) {
+      if (tk0 < m) red_add_f32(a.ws + (int64_t)tk0 * a.npad + row0, acc[n][0] * inv15 + s_out[warp][g][tk0]);
+      if (tk1 < m) red_add_f32(a.ws + (int64_t)tk1 * a.npad + row0, acc[n][1] * inv15 + s_out[warp][g][tk1]);
+    }
+    if (rv1) {
+      if (tk0 < m) red_add_f32(a.ws + (int64_t)tk0 * a.npad + row1, acc[n][2] * inv15 + s_out[warp][g + 8][tk0]);
+      if (tk1 < m) red_add_f32(a.ws + (int64_t)tk1 * a.npad + row1, acc[n][3] * inv15 + s_out[warp][g + 8][tk1]);
+    }
+  }
+  __threadfence();
+  __syncwarp();
+  int last = 0;
+  if (lane == 0) last = atomicAdd(a.counters + rt, 1) == 2 * a.n_chunks - 1;
+  last = __shfl_sync(0xffffffffu, last, 0);
+  if (!last) return;
+
+  // ---- epilogue of the row tile: bias, convert, store, clear the workspace ----
+  __threadfence();
+  for (int idx = lane; idx < 16 * m; idx += 32) {
+    const int tok = idx >> 4, r = idx & 15;
+    const int64_t row = rt * 16 + r;
+    if (row >= a.npad) continue;
+    float* wp = a.ws + (int64_t)tok * a.npad + row;
+    float v = __ldcg(wp);
+    __stcg(wp, 0.f);
+    if (row < a.n_out) {
+      if (a.bias) v += load_as_float(a.bias, a.bias_dtype, row);
+      store_from_float(a.y, a.y_dtype, (int64_t)tok * a.ldy + row, v);
+    }
+  }
+  if (lane == 0) a.counters[rt] = 0;
+}
+
+// ----------------------------------------------------------------------------------
+// outlier tiles: COO (ascending flat index) -> entries grouped by (row tile, chunk)
+// ----------------------------------------------------------------------------------
+struct CooView {
+  const int32_t* bidx;
+  const int32_t* off;
+  const uint16_t* val;
+  int64_t count, kpad, n_out, k_in;
+};
+
+__device__ __forceinline__ bool coo_decode(const CooView& c, int64_t i, int64_t& n, int64_t& k) {
+  const int64_t gi = (int64_t)c.bidx[i] * kBlock + c.off[i];
+  k = gi % c.kpad;
+  n = gi / c.kpad;
+  return k < c.k_in && n < c.n_out;
+}
+
+__global__ void outlier_hist_kernel(CooView c, int n_chunks, int32_t* cnt) {
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < c.count;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    int64_t n, k;
+    if (!coo_decode(c, i, n, k)) continue;
+    const int64_t tile = n >> 4, rit = n & 15, ch = k / (kChunkKb * kBlock);
+    atomicAdd(cnt + ((tile * n_chunks + ch) << 4) + rit, 1);
+  }
+}
+
+__global__ void outlier_segptr_kernel(const int32_t* dest, int64_t nseg, int32_t* seg_ptr) {
+  for (int64_t s = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; s <= nseg;
+       s += (int64_t)gridDim.x * blockDim.x)
+    seg_ptr[s] = dest[s << 4];          // dest has nseg*16 + 1 entries; [nseg*16] = total
+}
+
+__global__ void outlier_scatter_kernel(CooView c, int n_chunks, const int32_t* dest,
+                                       uint32_t* entries) {
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < c.count;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    int64_t n, k;
+    if (!coo_decode(c, i, n, k)) continue;
+    const int64_t ch = k / (kChunkKb * kBlock);
+    // first COO index of the (row n, chunk ch) run: binary search on the sorted flat index
+    const int64_t target = n * c.kpad + ch * (kChunkKb * kBlock);
+    int64_t lo = 0, hi = i;
+    while (lo < hi) {
+      const int64_t mid = (lo + hi) >> 1;
+      const int64_t gm = (int64_t)c.bidx[mid] * kBlock + c.off[mid];
+      if (gm < target) lo = mid + 1; else hi = mid;
+    }
+    const int64_t tile = n >> 4, rit = n & 15;
+    const int64_t pos = dest[((tile * n_chunks + ch) << 4) + rit] + (i - lo);
+    const uint32_t col = (uint32_t)(k - ch * (kChunkKb * kBlock));
+    entries[pos] = (uint32_t)c.val[i] | (col << 16) | ((uint32_t)rit << 26);
+  }
+}
+
+static int grid_for(int64_t work, int threads, int cap = 148 * 32) {
+  int64_t b = (work + threads - 1) / threads;
+  if (b > cap) b = cap;
+  return (int)(b < 1 ? 1 : b);
+}
+static size_t align256(size_t x) { return (x + 255) & ~(size_t)255; }
+
+}  // namespace fbfp
+
+using namespace fbfp;
+
+extern "C" int64_t fbfp_outlier_tiles_scratch_bytes(int64_t npad, int64_t kpad) {
+  const int64_t n_tiles = (npad + 15) / 16;
+  const int64_t n_chunks = (kpad / kBlock + kChunkKb - 1) / kChunkKb;
+  return (int64_t)align256(sizeof(int32_t) * (size_t)(n_tiles * n_chunks * 16 + 1));
+}
+
+extern "C" int fbfp_outlier_tiles_build(const int32_t* block_idx, const int32_t* offset,
+                                        const uint16_t* value_f16, int64_t count, int64_t kpad,
+                                        int64_t npad, int64_t n_out, int64_t k_in,
+                                        uint32_t* entries, int32_t* seg_ptr, void* scratch,
+                                        void* stream) {
+  FBFP_CHECK_ARG(seg_ptr && scratch, "null pointer");
+  FBFP_CHECK_ARG(count >= 0 && kpad > 0 && kpad % kBlock == 0 && npad >= n_out && n_out > 0 &&
+                 k_in > 0 && k_in <= kpad, "bad shape");
+  FBFP_CHECK_ARG(count == 0 || (block_idx && offset && value_f16 && entries), "null COO pointer");
+  cudaStream_t st = as_stream(stream);
+  const int64_t n_tiles = (npad + 15) / 16;
+  const int n_chunks = (int)((kpad / kBlock + kChunkKb - 1) / kChunkKb);
+  const int64_t nseg = n_tiles * n_chunks;
+  int32_t* dest = reinterpret_cast<int32_t*>(scratch);
+  FBFP_CUDA_TRY(cudaMemsetAsync(dest, 0, sizeof(int32_t) * (nseg * 16 + 1), st));
+  CooView c{block_idx, offset, value_f16, count, kpad, n_out, k_in};
+  if (count > 0) {
+    outlier_hist_kernel<<<grid_for(count, 256), 256, 0, st>>>(c, n_chunks, dest);
+    FBFP_LAUNCH_CHECK("outlier_hist_kernel");
+  }
+  scan_rows_kernel<<<1, 1024, 0, st>>>(dest, nseg * 16);
+  FBFP_LAUNCH_CHECK("scan_rows_kernel");
+  outlier_segptr_kernel<<<grid_for(nseg + 1, 256), 256, 0, st>>>(dest, nseg, seg_ptr);
+  FBFP_LAUNCH_CHECK("outlier_segptr_kernel");
+  if (count > 0) {
+    outlier_scatter_kernel<<<grid_for(count, 256), 256, 0, st>>>(c, n_chunks, dest, entries);
+    FBFP_LAUNCH_CHECK("outlier_scatter_kernel");
+  }
+  return FBFP_OK;
+}
+
+extern "C" int64_t fbfp_gemv_workspace_bytes(int64_t m, int64_t npad) {
+  const int64_t n_tiles = (npad + 15) / 16;
+  return (int64_t)(align256(sizeof(int32_t) * (size_t)n_tiles) +
+                   align256(sizeof(float) * (size_t)(m * npad)));
+}
+
+extern "C" int fbfp_gemv(const void* x, int x_dtype, int64_t m, int64_t ldx,
+                         const int8_t* exponents, const int16_t* signs, const int32_t* payload,
+                         int64_t n_out, int64_t k_in, int64_t kpad, int64_t npad,
+                         const uint32_t* entries, const int32_t* seg_ptr, const void* bias,
+                         int bias_dtype, void* y, int y_dtype, int64_t ldy, void* workspace,
+                         void* stream) {
+  FBFP_CHECK_ARG(x && exponents && signs && payload && y && workspace, "null pointer");
+  FBFP_CHECK_ARG(m >= 1 && m <= 16, "fbfp_gemv needs 1 <= m <= 16 (got %lld)", (long long)m);
+  FBFP_CHECK_ARG(dtype_ok(x_dtype), "x_dtype must be f32, bf16 or f16");
+  FBFP_CHECK_ARG(dtype_ok(y_dtype), "y_dtype must be f32, bf16 or f16");
+  FBFP_CHECK_ARG(!bias || dtype_ok(bias_dtype), "bad bias dtype");
+  FBFP_CHECK_ARG(n_out > 0 && k_in > 0 && kpad >= k_in && kpad % kBlock == 0 && npad >= n_out,
+                 "bad shape");
+  FBFP_CHECK_ARG(ldx >= k_in && ldy >= n_out, "bad leading dimension");
+  FBFP_CHECK_ARG(!entries || seg_ptr, "entries without seg_ptr");
+  FBFP_CHECK_ARG(((uintptr_t)payload & 7) == 0, "payload must be 8-byte aligned");
+  FBFP_CHECK_ARG(((uintptr_t)workspace & 255) == 0, "workspace must be 256-byte aligned");
+  const int64_t kb_row = kpad / kBlock;
+  const int n_chunks = (int)((kb_row + kChunkKb - 1) / kChunkKb);
+  const int64_t n_tiles = (npad + 15) / 16;
+  GemvArgs a;
+  a.x = x; a.x_dtype = x_dtype; a.m = (int)m; a.ldx = ldx;
+  a.ex = exponents; a.sg = reinterpret_cast<const uint16_t*>(signs);
+  a.pay = reinterpret_cast<const uint2*>(payload);
+  a.n_out = n_out; a.k_in = k_in; a.kb_row = kb_row; a.npad = npad;
+  a.entries = entries; a.seg_ptr = seg_ptr;
+  a.bias = bias; a.bias_dtype = bias_dtype;
+  a.y = y; a.y_dtype = y_dtype; a.ldy = ldy;
+  a.counters = reinterpret_cast<int32_t*>(workspace);
+  a.ws = reinterpret_cast<float*>(reinterpret_cast<char*>(workspace) +
+                                  align256(sizeof(int32_t) * (size_t)n_tiles));
+  a.n_chunks = n_chunks;
+  const dim3 grid((unsigned)((npad + kRowsPerCta - 1) / kRowsPerCta), (unsigned)n_chunks);
+  const size_t smem = sizeof(uint4) * 4 * (size_t)kChunkKb * (size_t)m;
+  cudaStream_t st = as_stream(stream);
+  if (m <= 8) {
+    if (smem > 48 * 1024)
+      FBFP_CUDA_TRY(cudaFuncSetAttribute(gemv_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+    gemv_kernel<1><<<grid, kGemvThreads, smem, st>>>(a);
+  } else {
+    if (smem > 48 * 1024)
+      FBFP_CUDA_TRY(cudaFuncSetAttribute(gemv_kernel<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+    gemv_kernel<2><<<grid, kGemvThreads, smem, st>>>(a);
+  }
+  FBFP_LAUNCH_CHECK("gemv_kernel");
+  return FBFP_OK;
+}

@@ -1,0 +1,248 @@
+"""``oabf_gemm`` and ``OABFLinear`` on B200 kernels.
+
+Mirrors flash_bfp/triton_kernel.py: ``oabf_gemm(X, dense_payload)`` (:130-195) returns the
+dense part ``X @ deq(W)^T`` (no outliers) in X's dtype; ``OABFLinear`` (:198-423) keeps the
+constructor, ``load_from_weight``, ``forward`` and the ``state_dict`` key layout. Unlike
+the reference there is no CPU fallback: inputs must be CUDA tensors and the CUDA library
+must be built, otherwise the call raises.
+
+Device-resident form of a layer (11 bytes per 16 weights + 4 bytes per outlier): the
+reference's packed bytes plus the outliers grouped for the fused kernels (``packed.py``).
+"""
+from __future__ import annotations
+
+from typing import Dict
+
+import torch
+
+from . import _lib
+from .compressor import padded_dims
+from .packed import PackedWeight, from_compressed
+
+# ------------------------------------------------------------------------------------
+# per-(device, stream) zero-initialised GEMV workspaces (the kernel leaves them zeroed)
+# ------------------------------------------------------------------------------------
+_WORKSPACES: Dict[tuple, torch.Tensor] = {}
+
+
+def gemv_workspace(device: torch.device, npad: int) -> torch.Tensor:
+    L = _lib.lib()
+    need = L.fbfp_gemv_workspace_bytes(16, npad)
+    key = (device.index, torch.cuda.current_stream(device).cuda_stream)
+    ws = _WORKSPACES.get(key)
+    if ws is None or ws.numel() < need:
+        ws = torch.zeros(need, dtype=torch.uint8, device=device)
+        _WORKSPACES[key] = ws
+    return ws
+
+
+def packed_linear(X: torch.Tensor, pw: PackedWeight, bias: torch.Tensor | None = None,
+                  out_dtype: torch.dtype | None = None, with_outliers: bool = True,
+                  out: torch.Tensor | None = None) -> torch.Tensor:
+    """Y[M, n_out] = X[M, k] @ W^T (+ outliers) (+ bias) through the CUDA kernels."""
+    L = _lib.lib()
+    _lib.require_cuda(X, "X")
+    if X.dim() != 2:
+        raise ValueError("packed_linear expects a 2-D X")
+    if X.stride(1) != 1:
+        X = X.contiguous()
+    M, Kx = X.shape
+    if Kx < pw.k_in:
+        raise ValueError(f"X has {Kx} columns, the weight needs {pw.k_in}")
+    out_dtype = out_dtype or X.dtype
+    xd = _lib.dtype_code(X.dtype, "X")
+    yd = _lib.dtype_code(out_dtype, "Y")
+    Y = out if out is not None else torch.empty(M, pw.n_out, dtype=out_dtype, device=X.device)
+    if M == 0:
+        return Y
+    use_out = with_outliers and pw.nnz > 0 and pw.entries is not None
+    entries = pw.entries if use_out else None
+    seg_ptr = pw.seg_ptr if use_out else None
+    bd = _lib.dtype_code(bias.dtype, "bias") if bias is not None else 0
+    ws = gemv_workspace(X.device, pw.npad)
+    st = _lib.stream_ptr(X.device)
+    for m0 in range(0, M, 16):
+        m = min(16, M - m0)
+        _lib.check(L.fbfp_gemv(_lib.ptr(X[m0:m0 + m]), xd, m, X.stride(0), _lib.ptr(pw.exps),
+                               _lib.ptr(pw.signs), _lib.ptr(pw.payload), pw.n_out, pw.k_in, pw.kpad,
+                               pw.npad, _lib.ptr(entries), _lib.ptr(seg_ptr), _lib.ptr(bias), bd,
+                               _lib.ptr(Y[m0:m0 + m]), yd, Y.stride(0), _lib.ptr(ws), st),
+                   "fbfp_gemv")
+    return Y
+
+
+def oabf_gemm(X: torch.Tensor, dense_payload: Dict) -> torch.Tensor:
+    """Dense part of the OABF product, ``X @ deq(W)^T`` in X's dtype (triton_kernel.py:130-195).
+
+    ``dense_payload`` is the compressor's dict; its tensors may live on the CPU (they are
+    copied to X's device) and may use the reference's widened GPU dtypes (fp32 exponents,
+    int32 signs, flat int32 payload; triton_kernel.py:101-110,147-158).
+    """
+    _lib.require_cuda(X, "X")
+    pw = from_compressed(dense_payload, None, X.device, build_tiles=False)
+    with torch.cuda.device(X.device):
+        return packed_linear(X, pw, None, X.dtype, with_outliers=False)
+
+
+class OABFLinear(torch.nn.Module):
+    def __init__(self, in_features: int, out_features: int, bias: bool = True):
+        super().__init__()
+        self.in_features = in_features
+        self.out_features = out_features
+        self.has_bias = bias
+        self.compressed = False
+        self._payload_meta = {}
+        self._sparse_meta = {}
+        # serialisation placeholders with the reference's names (triton_kernel.py:209-211);
+        # state_dict() fills them from the compact device form
+        self.register_buffer("_dp_exponents", torch.empty(0, dtype=torch.float32))
+        self.register_buffer("_sp_value", torch.empty(0, dtype=torch.float32))
+        if bias:
+            self.bias = torch.nn.Parameter(torch.zeros(out_features))
+        else:
+            self.register_parameter("bias", None)
+        self._pw: PackedWeight | None = None
+
+    def _apply(self, fn, *args, **kwargs):
+        super()._apply(fn, *args, **kwargs)
+        if self._pw is not None:
+            self._pw.apply(fn)                 # integer tensors: dtype casts leave them alone
+        return self
+
+    # -- triton_kernel.py:218-293 --------------------------------------------------------
+    def load_from_weight(self, W: torch.Tensor, compressor, device):
+        device = torch.device(device)
+        if device.type != "cuda":
+            raise RuntimeError("OABFLinear runs on a CUDA device (FlashBFP-B200 has no CPU path)")
+        if device.index is None:
+            device = torch.device("cuda", torch.cuda.current_device())
+        if W.device.type == "meta":
+            W = torch.zeros(W.shape, dtype=W.dtype)
+        with torch.cuda.device(device):
+            W = W.to(device)
+            if hasattr(compressor, "compress_matrix_device"):
+                dp, sp = compressor.compress_matrix_device(W)
+            else:
+                dp, sp = compressor.compress_matrix(W)
+        self.load_compressed(dp, sp, device)
+
+    def load_compressed(self, dp: Dict, sp: Dict, device) -> None:
+        """Adopt the compressor's (dense_payload, sparse_outliers) dicts."""
+        kpad, npad = dp["padded_shape"]
+        count = int(sp["count"])
+        if count:
+            b = sp["block_idx"].to(device).long()
+            o = sp["offset"].to(device).long()
+            g = b * 16 + o
+            if bool((b < 0).any()) or bool((o < 0).any()) or bool((o >= 16).any()) \
+                    or bool((g // kpad >= npad).any()):
+                raise IndexError("FlashBFP Compressor Error: outlier index out of padded bounds "
+                                 f"[0, {kpad - 1}] x [0, {npad - 1}]")
+        with torch.cuda.device(device):
+            pw = from_compressed(dp, sp, device, build_tiles=False)
+            pw.n_out, pw.k_in = self.out_features, self.in_features
+            pw.build_tiles()
+        self._pw = pw
+        self._payload_meta = {"padded_shape": (pw.kpad, pw.npad),
+                              "orig_shape": tuple(int(v) for v in dp["orig_shape"])}
+        self._sparse_meta = {"count": count}
+        self.compressed = True
+
+    @property
+    def packed(self) -> PackedWeight:
+        if not self.compressed:
+            raise RuntimeError("Weight matrix has not been compressed and loaded.")
+        return self._pw
+
+    # -- triton_kernel.py:295-368 --------------------------------------------------------
+    def forward(self, X: torch.Tensor) -> torch.Tensor:
+        if not self.compressed:
+            raise RuntimeError("Weight matrix has not been compressed and loaded.")
+        _lib.require_cuda(X, "X")
+        orig_shape = X.shape
+        in_dev = X.device
+        pw = self._pw
+        Xf = X.reshape(-1, self.in_features)
+        if Xf.device != pw.device:
+            Xf = Xf.to(pw.device)
+        bias = self.bias
+        if bias is not None and bias.device != pw.device:
+            bias = bias.to(pw.device)
+        out_dtype = X.dtype if bias is None else torch.promote_types(X.dtype, bias.dtype)
+        with torch.cuda.device(pw.device):
+            Y = packed_linear(Xf, pw, bias, out_dtype, with_outliers=True)
+        if Y.device != in_dev:
+            Y = Y.to(in_dev)
+        return Y.view(*orig_shape[:-1], self.out_features)
+
+    # -- triton_kernel.py:370-423: reference key layout ---------------------------------
+    def _reference_tensors(self):
+        pw = self._pw
+        out = {
+            "_dp_exponents": pw.exps.to(torch.float32),
+            "_dp_signs": pw.signs.to(torch.int32),
+            "_dp_payload": pw.payload.reshape(-1).clone(),
+        }
+        if pw.nnz:
+            bidx, off, val = pw.coo
+            g = bidx.long() * 16 + off.long()
+            r = g % pw.kpad
+            c = g // pw.kpad
+            keep = (r < self.in_features) & (c < self.out_features)
+            out["_sp_value"] = val.view(torch.float16).to(torch.float32)
+            out["_sp_r_idx"] = r[keep]
+            out["_sp_c_idx"] = c[keep]
+            out["_sp_v_val"] = val.view(torch.float16)[keep].to(torch.float32)
+        else:
+            out["_sp_value"] = torch.empty(0, dtype=torch.float32, device=pw.device)
+        return out
+
+    def state_dict(self, *args, destination=None, prefix="", keep_vars=False):
+        state = super().state_dict(destination=destination, prefix=prefix, keep_vars=keep_vars)
+        if self.compressed:
+            for k, v in self._reference_tensors().items():
+                state[prefix + k] = v
+        return state
+
+    def _load_from_state_dict(self, state_dict, prefix, local_metadata, strict, missing_keys,
+                              unexpected_keys, error_msgs):
+        keys = ["_dp_exponents", "_dp_signs", "_dp_payload", "_sp_value", "_sp_r_idx", "_sp_c_idx",
+                "_sp_v_val"]
+        got = {k: state_dict.pop(prefix + k) for k in keys if prefix + k in state_dict}
+        for k in ("_dp_exponents", "_sp_value"):       # let the placeholder buffers load empty
+            state_dict[prefix + k] = torch.empty(0, dtype=torch.float32)
+        super()._load_from_state_dict(state_dict, prefix, local_metadata, strict, missing_keys,
+                                      unexpected_keys, error_msgs)
+        for k in ("_dp_exponents", "_sp_value"):
+            state_dict.pop(prefix + k, None)
+        if not {"_dp_signs", "_dp_payload", "_dp_exponents"} <= set(got):
+            return
+        # padded shape from the layer dimensions with block 16 / tile 64 (triton_kernel.py:405-411)
+        kpad, npad = padded_dims(self.out_features, self.in_features, 16, 64)
+        if self._pw is not None:
+            device = self._pw.device
+        elif self.bias is not None and self.bias.is_cuda:
+            device = self.bias.device
+        else:
+            device = torch.device("cuda", torch.cuda.current_device())
+        dp = {
+            "exponents": got["_dp_exponents"].to(device),
+            "signs": got["_dp_signs"].to(device),
+            "payload": got["_dp_payload"].to(device),
+            "orig_shape": torch.Size((self.out_features, self.in_features)),
+            "padded_shape": (kpad, npad),
+        }
+        if "_sp_r_idx" in got:
+            r = got["_sp_r_idx"].to(device).long()
+            c = got["_sp_c_idx"].to(device).long()
+            g = c * kpad + r
+            order = torch.argsort(g)
+            g = g[order]
+            sp = {"block_idx": (g // 16).to(torch.int32), "offset": (g % 16).to(torch.int32),
+                  "value": got["_sp_v_val"].to(device)[order].to(torch.float16),
+                  "count": int(g.numel())}
+        else:
+            z = torch.zeros(0, dtype=torch.int32, device=device)
+            sp = {"block_idx": z, "offset": z.clone(),
+                  "value": torch.zeros(0, dtype=torch.float16, device=device), "count": 0}
+        self.load_compressed(dp, sp, device)

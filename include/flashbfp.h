@@ -1,0 +1,131 @@
+/*
+ * flashbfp.h — C ABI of libflashbfp.so, the B200 (sm_100a) OABF weight-streaming library.
+ *
+ * OABF (outlier-aware block floating point) packs a weight matrix W[N_out, K_in] as
+ * 16-element blocks along K: one int8 shared exponent, one 16-bit sign word and two
+ * 32-bit words of 4-bit mantissas per block (11 bytes per 16 weights), plus the
+ * values above an adaptive threshold as a COO list. Block b = n * (Kpad/16) + kb covers
+ * W[n, 16*kb : 16*kb + 16]. Packed arrays use exactly the byte layout of the reference
+ * compressor (Ragu-123/FlashBFP flash_bfp/compressor.py:109-117).
+ *
+ * Conventions for every entry point:
+ *   - all pointers are DEVICE pointers unless stated otherwise; sizes are element counts;
+ *   - `stream` is a cudaStream_t passed as void* (NULL = legacy default stream);
+ *   - the return value is an fbfp_status; FBFP_OK is 0. On error, fbfp_last_error()
+ *     returns a message for the calling thread. Nothing falls back to the CPU;
+ *   - calls only enqueue work on `stream` (no host synchronisation) unless stated.
+ */
+#ifndef FLASHBFP_H
+#define FLASHBFP_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+enum fbfp_status {
+  FBFP_OK = 0,
+  FBFP_ERR_ARG = 1,          /* invalid argument (null pointer, bad size, bad dtype)        */
+  FBFP_ERR_UNSUPPORTED = 2,  /* valid but unsupported configuration (e.g. block size != 16)  */
+  FBFP_ERR_CUDA = 3,         /* a CUDA runtime call or kernel launch failed                  */
+  FBFP_ERR_ALIGN = 4,        /* pointer alignment requirement not met                        */
+  FBFP_ERR_TIMEOUT = 5       /* a bounded device-side wait gave up                           */
+};
+
+enum fbfp_dtype { FBFP_F32 = 0, FBFP_BF16 = 1, FBFP_F16 = 2 };
+
+/* Library identity. */
+int fbfp_abi_version(void);
+const char* fbfp_status_string(int status);
+const char* fbfp_last_error(void);
+
+/* ------------------------------------------------------------------------------------
+ * Dequantisation (bit-exact).
+ * Replaces the dequantisation in _cpu_fallback_gemm (flash_bfp/triton_kernel.py:94-125)
+ * and in oabf_gemm_kernel (triton_kernel.py:68-80): w = (sign ? -1 : +1) * fl(m/15) * 2^e.
+ * Writes out[n * ldo + k] for n < n_out, k < k_in (the [:C_orig, :R_orig] crop). For
+ * out_dtype FBFP_BF16 the fp32 value is rounded to bf16, which equals both reference
+ * paths. sign=1 with m=0 gives -0.0 exactly as the reference formula does.
+ * ---------------------------------------------------------------------------------- */
+int fbfp_dequant(const int8_t* exponents, const int16_t* signs, const int32_t* payload,
+                 int64_t n_out, int64_t k_in, int64_t kpad,
+                 int out_dtype, void* out, int64_t ldo, void* stream);
+
+/* Write outliers into a dequantised matrix: out[c * ldo + r] = (float)value for every
+ * COO entry with r = g % kpad < k_in and c = g / kpad < n_out, g = block_idx*16 + offset.
+ * Follows the outlier re-insertion of flash_bfp main.py:100-113 and the index
+ * derivation of OABFLinear.load_from_weight (triton_kernel.py:261-277). `value_f16`
+ * holds IEEE half bit patterns. */
+int fbfp_scatter_outliers(const int32_t* block_idx, const int32_t* offset, const uint16_t* value_f16,
+                          int64_t count, int64_t kpad, int64_t n_out, int64_t k_in,
+                          int out_dtype, void* out, int64_t ldo, void* stream);
+
+/* ------------------------------------------------------------------------------------
+ * Outlier layout for the fused GEMV/GEMM (built once at load time).
+ * Replaces the (r, c, v) cache of OABFLinear.load_from_weight (triton_kernel.py:254-291).
+ * Entries are grouped by (16-row tile, 1024-column chunk); each entry is one uint32:
+ * bits 0-15 fp16 value, bits 16-25 column within the chunk, bits 26-29 row within the
+ * tile. seg_ptr has n_tiles * n_chunks + 1 entries (tile-major).
+ * fbfp_outlier_tiles_scratch_bytes gives the scratch size the build needs.
+ * ---------------------------------------------------------------------------------- */
+int64_t fbfp_outlier_tiles_scratch_bytes(int64_t npad, int64_t kpad);
+int fbfp_outlier_tiles_build(const int32_t* block_idx, const int32_t* offset, const uint16_t* value_f16,
+                             int64_t count, int64_t kpad, int64_t npad, int64_t n_out, int64_t k_in,
+                             uint32_t* entries, int32_t* seg_ptr, void* scratch, void* stream);
+
+/* ------------------------------------------------------------------------------------
+ * Fused dequant-GEMV for decode, 1 <= M <= 16 tokens.
+ * Replaces oabf_gemm (triton_kernel.py:130-195) for small M and, when `entries` is
+ * non-null, the outlier SpMV (triton_kernel.py:339-356) and bias add (:358-362) of
+ * OABFLinear.forward:  y[m, n] = sum_k x[m, k] * W_full[n, k] + bias[n], fp32 accumulate.
+ *   x: [M, K] row-major (leading dim ldx), dtype x_dtype (FBFP_BF16, FBFP_F32 or FBFP_F16;
+ *      fp32/fp16 activations are rounded to bf16 for the tensor-core product);
+ *   y: [M, n_out] row-major (leading dim ldy), dtype y_dtype (any fbfp_dtype);
+ *   bias: optional [n_out] of dtype bias_dtype (NULL for none);
+ *   workspace: fbfp_gemv_workspace_bytes(M, npad) bytes of ZERO-initialised device memory
+ *      (fp32 partial sums and arrival counters). The kernel returns it to zero before it
+ *      exits, so it can be reused by later calls on the same stream; concurrent calls
+ *      must use distinct workspaces.
+ * ---------------------------------------------------------------------------------- */
+int64_t fbfp_gemv_workspace_bytes(int64_t m, int64_t npad);
+int fbfp_gemv(const void* x, int x_dtype, int64_t m, int64_t ldx,
+              const int8_t* exponents, const int16_t* signs, const int32_t* payload,
+              int64_t n_out, int64_t k_in, int64_t kpad, int64_t npad,
+              const uint32_t* entries, const int32_t* seg_ptr,
+              const void* bias, int bias_dtype,
+              void* y, int y_dtype, int64_t ldy,
+              void* workspace, void* stream);
+
+/* ------------------------------------------------------------------------------------
+ * GPU compressor. Replaces OABFCompressor.compute_dynamic_threshold and
+ * compress_matrix (flash_bfp/compressor.py:11-117) with identical output bytes.
+ * w: [n_out, k_in] row-major (leading dim ldw) of dtype w_dtype (FBFP_F32 / FBFP_BF16);
+ * all arithmetic follows the reference's dtype-following torch semantics.
+ *
+ * Step 1, fbfp_compress_threshold: kurtosis-adaptive threshold written to *thr_out
+ *   (device float). scratch: fbfp_compress_scratch_bytes(...) bytes.
+ * Step 2, fbfp_compress_pack: packed exponents/signs/payload for the padded
+ *   [npad, kpad] matrix, the outlier bitmask per block (scratch) and per-row outlier
+ *   counts; then the exclusive scan of the row counts into row_offsets[npad + 1]
+ *   (row_offsets[npad] = total outlier count).
+ * Step 3, fbfp_compress_outliers: the COO list in ascending flat-index order
+ *   (block_idx, offset, fp16 value) into arrays of row_offsets[npad] entries.
+ * `thr` points to the device float threshold used by steps 2 and 3.
+ * ---------------------------------------------------------------------------------- */
+int64_t fbfp_compress_scratch_bytes(int64_t n_out, int64_t k_in, int64_t kpad, int64_t npad);
+int fbfp_compress_threshold(const void* w, int w_dtype, int64_t n_out, int64_t k_in, int64_t ldw,
+                            float* thr_out, void* scratch, void* stream);
+int fbfp_compress_pack(const void* w, int w_dtype, int64_t n_out, int64_t k_in, int64_t ldw,
+                       int64_t kpad, int64_t npad, const float* thr,
+                       int8_t* exponents, int16_t* signs, int32_t* payload,
+                       int32_t* row_offsets, void* scratch, void* stream);
+int fbfp_compress_outliers(const void* w, int w_dtype, int64_t n_out, int64_t k_in, int64_t ldw,
+                           int64_t kpad, int64_t npad, const int32_t* row_offsets,
+                           int32_t* block_idx, int32_t* offset, uint16_t* value_f16,
+                           void* scratch, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* FLASHBFP_H */
