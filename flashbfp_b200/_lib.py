@@ -33,6 +33,7 @@ _PROTOS = {
     "fbfp_outlier_tiles_build": (_c_int, [_vp, _vp, _vp, _c_i64, _c_i64, _c_i64, _c_i64, _c_i64,
                                           _vp, _vp, _vp, _vp]),
     "fbfp_gemv_workspace_bytes": (_c_i64, [_c_i64, _c_i64]),
+    "fbfp_gemv_check": (_c_int, [_vp, _vp]),
     "fbfp_gemv": (_c_int, [_vp, _c_int, _c_i64, _c_i64, _vp, _vp, _vp, _c_i64, _c_i64, _c_i64,
                            _c_i64, _vp, _vp, _vp, _c_int, _vp, _c_int, _c_i64, _vp, _vp]),
     "fbfp_compress_scratch_bytes": (_c_i64, [_c_i64, _c_i64, _c_i64, _c_i64]),

@@ -47,7 +47,7 @@ def build(force: bool = False, verbose: bool = False) -> str:
         subprocess.run(cmd, check=True)
         objs.append(obj)
     tmp = LIB + ".tmp"
-    cmd = [NVCC, *ARCH, "-shared", "-o", tmp, *objs, "-lcuda"]
+    cmd = [NVCC, *ARCH, "-shared", "-o", tmp, *objs]
     if verbose:
         print(" ".join(cmd), flush=True)
     subprocess.run(cmd, check=True)

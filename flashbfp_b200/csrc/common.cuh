@@ -74,7 +74,8 @@ inline int dtype_size(int d) { return d == FBFP_F32 ? 4 : 2; }
 #define FBFP_M15(m) ((float)(m) / 15.0f)
 
 constexpr int kBlock = 16;         // elements per OABF block
-constexpr int kChunkKb = 64;       // k-blocks per outlier chunk (1024 columns)
-constexpr int kTileRows = 16;      // rows per outlier tile / mma row tile
+constexpr int kChunkKb = 64;       // k-blocks per work chunk of the generic GEMV (1024 columns)
+constexpr int kGroupRows = 128;    // rows per outlier group / tcgen05 row group
+constexpr int kStageKb = 16;       // k-blocks per outlier stage / pipeline stage (256 columns)
 
 }  // namespace fbfp

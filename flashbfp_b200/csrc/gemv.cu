@@ -26,8 +26,13 @@
 // the two warps of that tile/chunk with shared-memory float atomics.
 #include "common.cuh"
 #include "scan.cuh"
+#include "tc_args.h"
 
 namespace fbfp {
+
+int launch_gemv_tc(const TcArgs& a, cudaStream_t st);
+bool gemv_tc_eligible(int64_t m, int64_t kb_row, int64_t k_in, int x_dtype, int64_t ldx, const void* x,
+                      const void* pay, const void* sg, const void* ex);
 
 constexpr int kGemvWarps = 8;
 constexpr int kGemvThreads = kGemvWarps * 32;
@@ -52,46 +57,73 @@ struct GemvArgs {
   float* ws;           // [m][npad] fp32 partial sums
   int32_t* counters;   // [ceil(npad/16)] arrivals per row tile
   int n_chunks;
+  bool vec;           // 16-byte vector loads of 8-block spans are legal
 };
 
 __device__ __forceinline__ void mma_bf16_16816(float (&d)[4], uint32_t a0, uint32_t a1,
                                                uint32_t a2, uint32_t a3, uint32_t b0,
                                                uint32_t b1) {
-  asm volatile(
+  asm(
       "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 "
       "{%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};\n"
       : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
       : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
 }
 
-__device__ __forceinline__ uint32_t ld_nc_u16(const uint16_t* p) {
-  unsigned short v;
-  asm volatile("ld.global.nc.u16 %0, [%1];\n" : "=h"(v) : "l"(p));
-  return v;
-}
-__device__ __forceinline__ int ld_nc_s8(const int8_t* p) {
-  short v;
-  asm volatile("ld.global.nc.s8 %0, [%1];\n" : "=h"(v) : "l"(p));
-  return v;
-}
-__device__ __forceinline__ uint2 ld_nc_u64(const uint2* p) {
-  uint2 v;
-  asm volatile("ld.global.nc.v2.u32 {%0,%1}, [%2];\n" : "=r"(v.x), "=r"(v.y) : "l"(p));
-  return v;
-}
 __device__ __forceinline__ void red_add_f32(float* p, float v) {
   asm volatile("red.global.add.f32 [%0], %1;\n" ::"l"(p), "f"(v) : "memory");
 }
 
 // Activation element position inside the staged chunk: element el (0..15) of k-block kbl,
 // token tok. Piece 0 holds pairs (0,4)(1,5)(2,6)(3,7), piece 1 pairs (8,12)..(11,15),
-// pieces 2/3 the negated copies; piece p of (kbl, tok) sits at slot p ^ (kbl & 3).
+// pieces 2/3 the negated copies. Lane t reads k-block 8t + j, so piece p of (kbl, tok) sits
+// at slot p ^ ((kbl >> 3) & 3): the four lanes of a quad hit four different bank groups.
 __device__ __forceinline__ int x_piece_slot(int kbl, int tok, int m, int piece) {
-  return ((kbl * m + tok) << 2) + (piece ^ (kbl & 3));
+  return ((kbl * m + tok) << 2) + (piece ^ ((kbl >> 3) & 3));
+}
+
+// Packed data of one row for the 8 consecutive blocks a lane owns.
+struct RowBlocks {
+  uint4 p[4];        // payload: p[c] = {w0, w1} of block 2c, {w0, w1} of block 2c+1
+  uint4 s;           // sign words, block j in halfword j
+  uint2 e;           // exponents, block j in byte j
+};
+
+__device__ __forceinline__ void load_row_blocks(const GemvArgs& a, int64_t row, int kbt, int nblk,
+                                                bool vec, RowBlocks& r) {
+  if (nblk == 8 && vec) {
+    const int64_t b = row * a.kb_row + kbt;
+    const uint4* pp = reinterpret_cast<const uint4*>(a.pay + b);
+#pragma unroll
+    for (int c = 0; c < 4; ++c) r.p[c] = __ldg(pp + c);
+    r.s = __ldg(reinterpret_cast<const uint4*>(a.sg + b));
+    r.e = __ldg(reinterpret_cast<const uint2*>(a.ex + b));
+    return;
+  }
+  uint32_t w[16], sw[4] = {0u, 0u, 0u, 0u}, ew[2] = {0u, 0u};
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    uint2 pj = make_uint2(0u, 0u);
+    uint32_t sj = 0u, ej = 0u;
+    if (j < nblk) {
+      const int64_t b = row * a.kb_row + kbt + j;
+      pj = __ldg(a.pay + b);
+      sj = __ldg(a.sg + b);
+      ej = (uint32_t)(uint8_t)__ldg(a.ex + b);
+    }
+    w[2 * j] = pj.x;
+    w[2 * j + 1] = pj.y;
+    sw[j >> 1] |= sj << (16 * (j & 1));
+    ew[j >> 2] |= ej << (8 * (j & 3));
+  }
+#pragma unroll
+  for (int c = 0; c < 4; ++c) r.p[c] = make_uint4(w[4 * c], w[4 * c + 1], w[4 * c + 2], w[4 * c + 3]);
+  r.s = make_uint4(sw[0], sw[1], sw[2], sw[3]);
+  r.e = make_uint2(ew[0], ew[1]);
 }
 
 template <int NT>
-__global__ void __launch_bounds__(kGemvThreads)
+__global__ void __launch_bounds__(kGemvThreads, 2)
 gemv_kernel(const GemvArgs a) {
   extern __shared__ uint4 xs[];                            // [64 kb][m][4] pieces
   __shared__ float s_out[kGemvWarps][16][16];              // outlier partials [row][token]
@@ -100,14 +132,29 @@ gemv_kernel(const GemvArgs a) {
   const int g = lane >> 2, t = lane & 3;
   const int m = a.m;
   const int chunk = blockIdx.y;
-  const int64_t kb_c0 = (int64_t)chunk * kChunkKb;
-  const int64_t kb_c1 = min(kb_c0 + kChunkKb, a.kb_row);
-  const int nkb = (int)(kb_c1 - kb_c0);
+  const int kb_c0 = chunk * kChunkKb;
+  const int kb_c1 = (int)min((int64_t)kb_c0 + kChunkKb, a.kb_row);
+  const int nkb = kb_c1 - kb_c0;
+
+  // ---- issue this lane's weight loads first: 8 blocks x 2 rows, independent of X ----
+  const int64_t rt = (int64_t)blockIdx.x * 4 + (warp & 3);
+  const bool tile_ok = rt * 16 < a.npad;
+  const int half = warp >> 2;
+  const int64_t row0 = rt * 16 + g, row1 = row0 + 8;
+  const bool rv0 = tile_ok && row0 < a.npad, rv1 = tile_ok && row1 < a.npad;
+  const int kb_lo = kb_c0 + half * kHalfKb;
+  const int kb_hi = min(kb_lo + kHalfKb, kb_c1);
+  const int kbt = kb_lo + 8 * t;                           // this lane's first block
+  const int nblk = max(0, min(8, kb_hi - kbt));
+  const bool vec = a.vec;
+  RowBlocks R0, R1;
+  load_row_blocks(a, row0, kbt, rv0 ? nblk : 0, vec, R0);
+  load_row_blocks(a, row1, kbt, rv1 ? nblk : 0, vec, R1);
 
   // ---- stage the activation chunk (bf16, permuted, with negated copy) ----
   for (int idx = threadIdx.x; idx < nkb * m; idx += kGemvThreads) {
     const int kbl = idx / m, tok = idx - kbl * m;
-    const int64_t k0 = (kb_c0 + kbl) * kBlock;
+    const int64_t k0 = (int64_t)(kb_c0 + kbl) * kBlock;
     uint32_t h[16];
     if (a.x_dtype == FBFP_BF16) {
       const uint16_t* xr = reinterpret_cast<const uint16_t*>(a.x) + tok * a.ldx + k0;
@@ -141,43 +188,38 @@ gemv_kernel(const GemvArgs a) {
   }
   for (int i = lane; i < 256; i += 32) (&s_out[warp][0][0])[i] = 0.f;
   __syncthreads();
-
-  const int64_t rt = (int64_t)blockIdx.x * 4 + (warp & 3);
-  if (rt * 16 >= a.npad) return;                          // row tile past the matrix
-  const int half = warp >> 2;
-  const int64_t row0 = rt * 16 + g, row1 = row0 + 8;
-  const bool rv0 = row0 < a.npad, rv1 = row1 < a.npad;
-  const int64_t kb_lo = kb_c0 + half * kHalfKb;
-  const int64_t kb_hi = min(kb_lo + kHalfKb, kb_c1);
+  if (!tile_ok) return;                                     // row tile past the matrix
 
   float acc[NT][4];
 #pragma unroll
   for (int n = 0; n < NT; ++n) acc[n][0] = acc[n][1] = acc[n][2] = acc[n][3] = 0.f;
 
-  const int64_t base0 = row0 * a.kb_row, base1 = row1 * a.kb_row;
-  for (int64_t kb4 = kb_lo; kb4 < kb_hi; kb4 += 4) {
-    const int64_t kb = kb4 + t;
-    const bool ok = kb < kb_hi;
-    const bool ok0 = ok && rv0, ok1 = ok && rv1;
-    const uint2 p0 = ok0 ? ld_nc_u64(a.pay + base0 + kb) : make_uint2(0u, 0u);
-    const uint2 p1 = ok1 ? ld_nc_u64(a.pay + base1 + kb) : make_uint2(0u, 0u);
-    const uint32_t s0 = ok0 ? ld_nc_u16(a.sg + base0 + kb) : 0u;
-    const uint32_t s1 = ok1 ? ld_nc_u16(a.sg + base1 + kb) : 0u;
-    const int e0 = ok0 ? ld_nc_s8(a.ex + base0 + kb) : 0;
-    const int e1 = ok1 ? ld_nc_s8(a.ex + base1 + kb) : 0;
-    // bf16 exponent field of 128 * 2^e in both halves (zero for an absent block)
-    const uint32_t K0 = ok0 ? (uint32_t)(e0 + 134) * 0x00800080u : 0u;
-    const uint32_t K1 = ok1 ? (uint32_t)(e1 + 134) * 0x00800080u : 0u;
-    // sign bit j at j and j + 12: pair (q, q+4) lands on bits 15/31 after << (15 - q),
-    // pair (q+8, q+12) after << (7 - q)
+  // exponent bytes -> e + 134 per byte without carries (e in [-128, 121])
+  const uint32_t E0lo = (R0.e.x ^ 0x80808080u) + 0x06060606u, E0hi = (R0.e.y ^ 0x80808080u) + 0x06060606u;
+  const uint32_t E1lo = (R1.e.x ^ 0x80808080u) + 0x06060606u, E1hi = (R1.e.y ^ 0x80808080u) + 0x06060606u;
+  const uint32_t sw0[4] = {R0.s.x, R0.s.y, R0.s.z, R0.s.w};
+  const uint32_t sw1[4] = {R1.s.x, R1.s.y, R1.s.z, R1.s.w};
+  const int kbl0 = kbt - kb_c0;
+
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    const uint4 P0 = R0.p[j >> 1], P1 = R1.p[j >> 1];
+    const uint32_t w00 = (j & 1) ? P0.z : P0.x, w01 = (j & 1) ? P0.w : P0.y;   // row g
+    const uint32_t w10 = (j & 1) ? P1.z : P1.x, w11 = (j & 1) ? P1.w : P1.y;   // row g+8
+    const uint32_t s0 = (j & 1) ? (sw0[j >> 1] >> 16) : (sw0[j >> 1] & 0xFFFFu);
+    const uint32_t s1 = (j & 1) ? (sw1[j >> 1] >> 16) : (sw1[j >> 1] & 0xFFFFu);
     const uint32_t y0 = s0 | (s0 << 12), y1 = s1 | (s1 << 12);
+    const uint32_t eb0 = (((j < 4) ? E0lo : E0hi) >> (8 * (j & 3))) & 0xFFu;
+    const uint32_t eb1 = (((j < 4) ? E1lo : E1hi) >> (8 * (j & 3))) & 0xFFu;
+    const uint32_t K0 = eb0 * 0x00800080u, K1 = eb1 * 0x00800080u;
+    const bool valid = j < nblk;
 
     uint32_t xv[NT][8], xn[NT][8];
-    const int kbl = (int)(kb - kb_c0);
+    const int kbl = kbl0 + j;
 #pragma unroll
     for (int n = 0; n < NT; ++n) {
       const int tok = n * 8 + g;
-      if (ok && tok < m) {
+      if (valid && tok < m) {
         const uint4 q0 = xs[x_piece_slot(kbl, tok, m, 0)];
         const uint4 q1 = xs[x_piece_slot(kbl, tok, m, 1)];
         const uint4 q2 = xs[x_piece_slot(kbl, tok, m, 2)];
@@ -188,7 +230,7 @@ gemv_kernel(const GemvArgs a) {
         xn[n][4] = q3.x; xn[n][5] = q3.y; xn[n][6] = q3.z; xn[n][7] = q3.w;
       } else {
 #pragma unroll
-        for (int j = 0; j < 8; ++j) { xv[n][j] = 0u; xn[n][j] = 0u; }
+        for (int i = 0; i < 8; ++i) { xv[n][i] = 0u; xn[n][i] = 0u; }
       }
     }
 #pragma unroll
@@ -198,10 +240,10 @@ gemv_kernel(const GemvArgs a) {
       const uint32_t cB0 = ((y0 << (7 - q)) & SM) | K0;    // row g,   elements q+8, q+12
       const uint32_t cA1 = ((y1 << (15 - q)) & SM) | K1;   // row g+8
       const uint32_t cB1 = ((y1 << (7 - q)) & SM) | K1;
-      const uint32_t vA0 = ((p0.x >> (4 * q)) & NM) | cA0;
-      const uint32_t vB0 = ((p0.y >> (4 * q)) & NM) | cB0;
-      const uint32_t vA1 = ((p1.x >> (4 * q)) & NM) | cA1;
-      const uint32_t vB1 = ((p1.y >> (4 * q)) & NM) | cB1;
+      const uint32_t vA0 = ((w00 >> (4 * q)) & NM) | cA0;
+      const uint32_t vB0 = ((w01 >> (4 * q)) & NM) | cB0;
+      const uint32_t vA1 = ((w10 >> (4 * q)) & NM) | cA1;
+      const uint32_t vB1 = ((w11 >> (4 * q)) & NM) | cB1;
 #pragma unroll
       for (int n = 0; n < NT; ++n) {
         mma_bf16_16816(acc[n], vA0, vA1, vB0, vB1, xv[n][q], xv[n][4 + q]);
@@ -210,21 +252,29 @@ gemv_kernel(const GemvArgs a) {
     }
   }
 
-  // ---- outliers of this (row tile, chunk), split between the two half-warps ----
+  // ---- outliers of this row tile in this warp's 32 k-blocks: the (128-row group,
+  //      16-block stage) segments covering them, filtered to the tile's 16 rows ----
   if (a.entries) {
-    const int seg = (int)(rt * a.n_chunks + chunk);
-    const int lo = a.seg_ptr[seg], hi = a.seg_ptr[seg + 1];
+    const int64_t rg = rt / 8;
+    const int r_lo = (int)(rt % 8) * 16;
+    const int n_stages = (int)((a.kb_row + kStageKb - 1) / kStageKb);
     const uint16_t* xh = reinterpret_cast<const uint16_t*>(xs);
-    for (int i = lo + half * 32 + lane; i < hi; i += 64) {
-      const uint32_t e = __ldg(a.entries + i);
-      const float v = __half2float(__ushort_as_half((unsigned short)(e & 0xFFFF)));
-      const int col = (e >> 16) & 0x3FF, r = (e >> 26) & 0xF;
-      const int kbl = col >> 4, el = col & 15;
-      const int piece = el >> 3, e7 = el & 7;
-      const int pos = ((e7 & 3) << 1) + (e7 >> 2);
-      for (int tok = 0; tok < m; ++tok) {
-        const float xv = bf16_bits_to_float(xh[x_piece_slot(kbl, tok, m, piece) * 8 + pos]);
-        atomicAdd(&s_out[warp][r][tok], v * xv);
+    for (int st = kb_lo / kStageKb; st * kStageKb < kb_hi; ++st) {
+      const int64_t seg = rg * n_stages + st;
+      const int lo = a.seg_ptr[seg], hi = a.seg_ptr[seg + 1];
+      for (int i = lo + lane; i < hi; i += 32) {
+        const uint32_t e = __ldg(a.entries + i);
+        const int r = (int)(e >> 24) - r_lo;
+        if (r < 0 || r >= 16) continue;
+        const float v = __half2float(__ushort_as_half((unsigned short)(e & 0xFFFF)));
+        const int col = st * kStageKb * kBlock + (int)((e >> 16) & 0xFF) - kb_c0 * kBlock;
+        const int kbl = col >> 4, el = col & 15;
+        const int piece = el >> 3, e7 = el & 7;
+        const int pos = ((e7 & 3) << 1) + (e7 >> 2);
+        for (int tok = 0; tok < m; ++tok) {
+          const float xv = bf16_bits_to_float(xh[x_piece_slot(kbl, tok, m, piece) * 8 + pos]);
+          atomicAdd(&s_out[warp][r][tok], v * xv);
+        }
       }
     }
     __syncwarp();
@@ -268,113 +318,35 @@ gemv_kernel(const GemvArgs a) {
   if (lane == 0) a.counters[rt] = 0;
 }
 
-// ----------------------------------------------------------------------------------
-// outlier tiles: COO (ascending flat index) -> entries grouped by (row tile, chunk)
-// ----------------------------------------------------------------------------------
-struct CooView {
-  const int32_t* bidx;
-  const int32_t* off;
-  const uint16_t* val;
-  int64_t count, kpad, n_out, k_in;
-};
-
-__device__ __forceinline__ bool coo_decode(const CooView& c, int64_t i, int64_t& n, int64_t& k) {
-  const int64_t gi = (int64_t)c.bidx[i] * kBlock + c.off[i];
-  k = gi % c.kpad;
-  n = gi / c.kpad;
-  return k < c.k_in && n < c.n_out;
-}
-
-__global__ void outlier_hist_kernel(CooView c, int n_chunks, int32_t* cnt) {
-  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < c.count;
-       i += (int64_t)gridDim.x * blockDim.x) {
-    int64_t n, k;
-    if (!coo_decode(c, i, n, k)) continue;
-    const int64_t tile = n >> 4, rit = n & 15, ch = k / (kChunkKb * kBlock);
-    atomicAdd(cnt + ((tile * n_chunks + ch) << 4) + rit, 1);
-  }
-}
-
-__global__ void outlier_segptr_kernel(const int32_t* dest, int64_t nseg, int32_t* seg_ptr) {
-  for (int64_t s = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; s <= nseg;
-       s += (int64_t)gridDim.x * blockDim.x)
-    seg_ptr[s] = dest[s << 4];          // dest has nseg*16 + 1 entries; [nseg*16] = total
-}
-
-__global__ void outlier_scatter_kernel(CooView c, int n_chunks, const int32_t* dest,
-                                       uint32_t* entries) {
-  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < c.count;
-       i += (int64_t)gridDim.x * blockDim.x) {
-    int64_t n, k;
-    if (!coo_decode(c, i, n, k)) continue;
-    const int64_t ch = k / (kChunkKb * kBlock);
-    // first COO index of the (row n, chunk ch) run: binary search on the sorted flat index
-    const int64_t target = n * c.kpad + ch * (kChunkKb * kBlock);
-    int64_t lo = 0, hi = i;
-    while (lo < hi) {
-      const int64_t mid = (lo + hi) >> 1;
-      const int64_t gm = (int64_t)c.bidx[mid] * kBlock + c.off[mid];
-      if (gm < target) lo = mid + 1; else hi = mid;
-    }
-    const int64_t tile = n >> 4, rit = n & 15;
-    const int64_t pos = dest[((tile * n_chunks + ch) << 4) + rit] + (i - lo);
-    const uint32_t col = (uint32_t)(k - ch * (kChunkKb * kBlock));
-    entries[pos] = (uint32_t)c.val[i] | (col << 16) | ((uint32_t)rit << 26);
-  }
-}
-
-static int grid_for(int64_t work, int threads, int cap = 148 * 32) {
-  int64_t b = (work + threads - 1) / threads;
-  if (b > cap) b = cap;
-  return (int)(b < 1 ? 1 : b);
-}
 static size_t align256(size_t x) { return (x + 255) & ~(size_t)255; }
 
 }  // namespace fbfp
 
 using namespace fbfp;
 
-extern "C" int64_t fbfp_outlier_tiles_scratch_bytes(int64_t npad, int64_t kpad) {
-  const int64_t n_tiles = (npad + 15) / 16;
-  const int64_t n_chunks = (kpad / kBlock + kChunkKb - 1) / kChunkKb;
-  return (int64_t)align256(sizeof(int32_t) * (size_t)(n_tiles * n_chunks * 16 + 1));
-}
-
-extern "C" int fbfp_outlier_tiles_build(const int32_t* block_idx, const int32_t* offset,
-                                        const uint16_t* value_f16, int64_t count, int64_t kpad,
-                                        int64_t npad, int64_t n_out, int64_t k_in,
-                                        uint32_t* entries, int32_t* seg_ptr, void* scratch,
-                                        void* stream) {
-  FBFP_CHECK_ARG(seg_ptr && scratch, "null pointer");
-  FBFP_CHECK_ARG(count >= 0 && kpad > 0 && kpad % kBlock == 0 && npad >= n_out && n_out > 0 &&
-                 k_in > 0 && k_in <= kpad, "bad shape");
-  FBFP_CHECK_ARG(count == 0 || (block_idx && offset && value_f16 && entries), "null COO pointer");
-  cudaStream_t st = as_stream(stream);
-  const int64_t n_tiles = (npad + 15) / 16;
-  const int n_chunks = (int)((kpad / kBlock + kChunkKb - 1) / kChunkKb);
-  const int64_t nseg = n_tiles * n_chunks;
-  int32_t* dest = reinterpret_cast<int32_t*>(scratch);
-  FBFP_CUDA_TRY(cudaMemsetAsync(dest, 0, sizeof(int32_t) * (nseg * 16 + 1), st));
-  CooView c{block_idx, offset, value_f16, count, kpad, n_out, k_in};
-  if (count > 0) {
-    outlier_hist_kernel<<<grid_for(count, 256), 256, 0, st>>>(c, n_chunks, dest);
-    FBFP_LAUNCH_CHECK("outlier_hist_kernel");
-  }
-  scan_rows_kernel<<<1, 1024, 0, st>>>(dest, nseg * 16);
-  FBFP_LAUNCH_CHECK("scan_rows_kernel");
-  outlier_segptr_kernel<<<grid_for(nseg + 1, 256), 256, 0, st>>>(dest, nseg, seg_ptr);
-  FBFP_LAUNCH_CHECK("outlier_segptr_kernel");
-  if (count > 0) {
-    outlier_scatter_kernel<<<grid_for(count, 256), 256, 0, st>>>(c, n_chunks, dest, entries);
-    FBFP_LAUNCH_CHECK("outlier_scatter_kernel");
-  }
-  return FBFP_OK;
+// Workspace layout: [error word + pad: 256 B][arrival counters: ceil(npad/16) int32]
+// [fp32 partial sums: m x npad]; every region is zero between calls, so one workspace
+// sized for the largest npad serves matrices of any smaller size.
+static size_t ws_counters_bytes(int64_t npad) {
+  return align256(sizeof(int32_t) * (size_t)((npad + 15) / 16));
 }
 
 extern "C" int64_t fbfp_gemv_workspace_bytes(int64_t m, int64_t npad) {
-  const int64_t n_tiles = (npad + 15) / 16;
-  return (int64_t)(align256(sizeof(int32_t) * (size_t)n_tiles) +
-                   align256(sizeof(float) * (size_t)(m * npad)));
+  return (int64_t)(256 + ws_counters_bytes(npad) + align256(sizeof(float) * (size_t)(m * npad)));
+}
+
+extern "C" int fbfp_gemv_check(void* workspace, void* stream) {
+  FBFP_CHECK_ARG(workspace, "null workspace");
+  cudaStream_t st = as_stream(stream);
+  int32_t* errp = reinterpret_cast<int32_t*>(workspace);
+  int32_t h = 0;
+  FBFP_CUDA_TRY(cudaMemcpyAsync(&h, errp, sizeof(h), cudaMemcpyDeviceToHost, st));
+  FBFP_CUDA_TRY(cudaStreamSynchronize(st));
+  if (h != 0) {
+    FBFP_CUDA_TRY(cudaMemsetAsync(errp, 0, sizeof(int32_t), st));
+    return set_error(FBFP_ERR_TIMEOUT, "a bounded device-side wait gave up (site %d)", (int)h);
+  }
+  return FBFP_OK;
 }
 
 extern "C" int fbfp_gemv(const void* x, int x_dtype, int64_t m, int64_t ldx,
@@ -396,7 +368,6 @@ extern "C" int fbfp_gemv(const void* x, int x_dtype, int64_t m, int64_t ldx,
   FBFP_CHECK_ARG(((uintptr_t)workspace & 255) == 0, "workspace must be 256-byte aligned");
   const int64_t kb_row = kpad / kBlock;
   const int n_chunks = (int)((kb_row + kChunkKb - 1) / kChunkKb);
-  const int64_t n_tiles = (npad + 15) / 16;
   GemvArgs a;
   a.x = x; a.x_dtype = x_dtype; a.m = (int)m; a.ldx = ldx;
   a.ex = exponents; a.sg = reinterpret_cast<const uint16_t*>(signs);
@@ -405,13 +376,28 @@ extern "C" int fbfp_gemv(const void* x, int x_dtype, int64_t m, int64_t ldx,
   a.entries = entries; a.seg_ptr = seg_ptr;
   a.bias = bias; a.bias_dtype = bias_dtype;
   a.y = y; a.y_dtype = y_dtype; a.ldy = ldy;
-  a.counters = reinterpret_cast<int32_t*>(workspace);
-  a.ws = reinterpret_cast<float*>(reinterpret_cast<char*>(workspace) +
-                                  align256(sizeof(int32_t) * (size_t)n_tiles));
+  int32_t* errp = reinterpret_cast<int32_t*>(workspace);
+  a.counters = reinterpret_cast<int32_t*>(reinterpret_cast<char*>(workspace) + 256);
+  a.ws = reinterpret_cast<float*>(reinterpret_cast<char*>(workspace) + 256 + ws_counters_bytes(npad));
   a.n_chunks = n_chunks;
+  a.vec = (kb_row % 8 == 0) && ((uintptr_t)payload % 16 == 0) && ((uintptr_t)signs % 16 == 0) &&
+          ((uintptr_t)exponents % 8 == 0);
+  cudaStream_t st = as_stream(stream);
+  if (gemv_tc_eligible(m, kb_row, k_in, x_dtype, ldx, x, payload, signs, exponents)) {
+    TcArgs t;
+    t.x = x; t.x_dtype = x_dtype; t.m = (int)m; t.ldx = ldx;
+    t.ex = exponents; t.sg = reinterpret_cast<const uint16_t*>(signs);
+    t.pay = reinterpret_cast<const uint2*>(payload);
+    t.n_out = n_out; t.k_in = k_in; t.kb_row = kb_row; t.npad = npad;
+    t.entries = entries; t.seg_ptr = seg_ptr; t.bias = bias; t.bias_dtype = bias_dtype;
+    t.y = y; t.y_dtype = y_dtype; t.ldy = ldy;
+    t.ws = a.ws; t.counters = a.counters; t.err = errp;
+    t.n_stages = (int)(kb_row / kStageKb);
+    t.total_units = ((npad + kGroupRows - 1) / kGroupRows) * t.n_stages;
+    return launch_gemv_tc(t, st);
+  }
   const dim3 grid((unsigned)((npad + kRowsPerCta - 1) / kRowsPerCta), (unsigned)n_chunks);
   const size_t smem = sizeof(uint4) * 4 * (size_t)kChunkKb * (size_t)m;
-  cudaStream_t st = as_stream(stream);
   if (m <= 8) {
     if (smem > 48 * 1024)
       FBFP_CUDA_TRY(cudaFuncSetAttribute(gemv_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));

@@ -36,6 +36,16 @@ def gemv_workspace(device: torch.device, npad: int) -> torch.Tensor:
     return ws
 
 
+def check_device_errors(device=None) -> None:
+    """Synchronise and raise if a GEMV on `device` gave up a bounded device-side wait."""
+    L = _lib.lib()
+    for (idx, sptr), ws in list(_WORKSPACES.items()):
+        if device is not None and torch.device(device).index != idx:
+            continue
+        with torch.cuda.device(idx):
+            _lib.check(L.fbfp_gemv_check(_lib.ptr(ws), _lib.ctypes.c_void_p(sptr)), "fbfp_gemv_check")
+
+
 def packed_linear(X: torch.Tensor, pw: PackedWeight, bias: torch.Tensor | None = None,
                   out_dtype: torch.dtype | None = None, with_outliers: bool = True,
                   out: torch.Tensor | None = None) -> torch.Tensor:

@@ -3,7 +3,7 @@
 A ``PackedWeight`` holds the reference's packed arrays on the device — exponents
 int8[npad*kb], signs int16[npad*kb], payload int32[npad*kb, 2], block b = n*kb + j — plus
 the outlier list in COO form (block index, offset, fp16 bits; ascending flat order) and in
-the (16-row tile, 1024-column chunk) form the fused kernels read.
+the (128-row group, 256-column stage) form the fused kernels read.
 
 Row concatenation serves fused launches (q|k|v, gate|up share their input); row and
 block-column slices serve tensor parallelism. Because the outlier threshold is a
@@ -56,10 +56,10 @@ class PackedWeight:
         L = _lib.lib()
         dev = self.device
         count = self.nnz
-        n_tiles = (self.npad + 15) // 16
-        n_chunks = (self.kb_row + 63) // 64
+        n_groups = (self.npad + 127) // 128
+        n_stages = (self.kb_row + 15) // 16
         entries = torch.empty(max(count, 1), dtype=torch.int32, device=dev)
-        seg_ptr = torch.empty(n_tiles * n_chunks + 1, dtype=torch.int32, device=dev)
+        seg_ptr = torch.empty(n_groups * n_stages + 1, dtype=torch.int32, device=dev)
         scratch = torch.empty(L.fbfp_outlier_tiles_scratch_bytes(self.npad, self.kpad),
                               dtype=torch.uint8, device=dev)
         b, o, v = self.coo if count else (None, None, None)

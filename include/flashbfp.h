@@ -64,9 +64,11 @@ int fbfp_scatter_outliers(const int32_t* block_idx, const int32_t* offset, const
 /* ------------------------------------------------------------------------------------
  * Outlier layout for the fused GEMV/GEMM (built once at load time).
  * Replaces the (r, c, v) cache of OABFLinear.load_from_weight (triton_kernel.py:254-291).
- * Entries are grouped by (16-row tile, 1024-column chunk); each entry is one uint32:
- * bits 0-15 fp16 value, bits 16-25 column within the chunk, bits 26-29 row within the
- * tile. seg_ptr has n_tiles * n_chunks + 1 entries (tile-major).
+ * Entries are grouped by (128-row group, 256-column stage); each entry is one uint32:
+ * bits 0-15 fp16 value, bits 16-23 column within the stage, bits 24-30 row within the
+ * group. seg_ptr has n_groups * n_stages + 1 entries (group-major), n_groups =
+ * ceil(npad/128), n_stages = ceil(kpad/256); the count argument must list the COO entries
+ * in ascending flat-index order, as the compressor emits them.
  * fbfp_outlier_tiles_scratch_bytes gives the scratch size the build needs.
  * ---------------------------------------------------------------------------------- */
 int64_t fbfp_outlier_tiles_scratch_bytes(int64_t npad, int64_t kpad);
@@ -84,11 +86,16 @@ int fbfp_outlier_tiles_build(const int32_t* block_idx, const int32_t* offset, co
  *   y: [M, n_out] row-major (leading dim ldy), dtype y_dtype (any fbfp_dtype);
  *   bias: optional [n_out] of dtype bias_dtype (NULL for none);
  *   workspace: fbfp_gemv_workspace_bytes(M, npad) bytes of ZERO-initialised device memory
- *      (fp32 partial sums and arrival counters). The kernel returns it to zero before it
- *      exits, so it can be reused by later calls on the same stream; concurrent calls
- *      must use distinct workspaces.
+ *      (error word, arrival counters, fp32 partial sums). The kernel returns it to zero
+ *      before it exits, so it can be reused by later calls on the same stream, also for
+ *      smaller matrices; concurrent calls must use distinct workspaces.
+ * Matrices with kpad a multiple of 256 (16 blocks per row stage) and 16-byte aligned
+ * packed arrays run on the persistent tcgen05 kernel; other shapes on the mma.sync kernel.
  * ---------------------------------------------------------------------------------- */
 int64_t fbfp_gemv_workspace_bytes(int64_t m, int64_t npad);
+/* Synchronises `stream` and reports FBFP_ERR_TIMEOUT if a kernel that used `workspace`
+ * gave up a bounded device-side wait since the last check (then clears the record). */
+int fbfp_gemv_check(void* workspace, void* stream);
 int fbfp_gemv(const void* x, int x_dtype, int64_t m, int64_t ldx,
               const int8_t* exponents, const int16_t* signs, const int32_t* payload,
               int64_t n_out, int64_t k_in, int64_t kpad, int64_t npad,

@@ -232,7 +232,8 @@ def test_linear_vs_reference_forward(name):
 
 
 @pytest.mark.parametrize("m", [1, 2, 3, 4, 7, 8, 9, 15, 16, 17, 40])
-@pytest.mark.parametrize("shape", [(192, 256), (100, 70), (4096, 3840), (3840, 4096)])
+@pytest.mark.parametrize("shape", [(192, 256), (100, 70), (4096, 3840), (3840, 4096), (200, 3856),
+                                   (3840, 15360)])
 def test_linear_vs_torch_fp32(m, shape):
     """OABFLinear vs a plain PyTorch fp32 dequantize-then-matmul of the same weights."""
     from flashbfp_b200 import OABFCompressor, OABFLinear, workloads
@@ -245,6 +246,8 @@ def test_linear_vs_torch_fp32(m, shape):
     Wf = _dequant_full(dp, sp)
     X = workloads.activations(m, k, seed=m, device="cuda")
     Y = lin(X)
+    from flashbfp_b200.linear import check_device_errors
+    check_device_errors()
     ref = X.float() @ Wf.t()
     rel = ((Y.float() - ref).norm() / ref.norm()).item()
     assert rel <= GEMM_TOL, rel
