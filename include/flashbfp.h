@@ -104,6 +104,25 @@ int fbfp_gemv(const void* x, int x_dtype, int64_t m, int64_t ldx,
               void* y, int y_dtype, int64_t ldy,
               void* workspace, void* stream);
 
+/* fbfp_gemv without a caller workspace. No counterpart in the reference: it exists for
+ * callers that cannot allocate device memory — a plugin inside a host application that owns
+ * all GPU memory through its own pool and forbids stray cudaMalloc calls, or a thin
+ * foreign-language binding with no device allocator to hand over a workspace.
+ * Same arguments and results as fbfp_gemv, minus `workspace`: the scratch lives in an 8 MiB
+ * array compiled into the library (every GPU that loads the library holds it until exit).
+ * Returns FBFP_ERR_ARG when fbfp_gemv_workspace_bytes(m, npad) exceeds 8 MiB (about 130,000
+ * padded rows at m = 16). Allocates nothing; each call clears the part of the array it uses.
+ * The first call on a device looks up the array's device address (cudaGetSymbolAddress):
+ * make that first call outside any stream capture. All calls on a device share the one
+ * array, so calls that overlap on the GPU (other streams, other host threads) race and
+ * corrupt each other's results: serialise them. */
+int fbfp_gemv_noalloc(const void* x, int x_dtype, int64_t m, int64_t ldx,
+                      const int8_t* exponents, const int16_t* signs, const int32_t* payload,
+                      int64_t n_out, int64_t k_in, int64_t kpad, int64_t npad,
+                      const uint32_t* entries, const int32_t* seg_ptr,
+                      const void* bias, int bias_dtype,
+                      void* y, int y_dtype, int64_t ldy, void* stream);
+
 /* ------------------------------------------------------------------------------------
  * GPU compressor. Replaces OABFCompressor.compute_dynamic_threshold and
  * compress_matrix (flash_bfp/compressor.py:11-117) with identical output bytes.
