@@ -30,6 +30,7 @@ _PROTOS = {
     "fbfp_scatter_outliers": (_c_int, [_vp, _vp, _vp, _c_i64, _c_i64, _c_i64, _c_i64, _c_int, _vp,
                                        _c_i64, _vp]),
     "fbfp_outlier_tiles_scratch_bytes": (_c_i64, [_c_i64, _c_i64]),
+    "fbfp_outlier_tiles_index_words": (_c_i64, [_c_i64, _c_i64]),
     "fbfp_outlier_tiles_build": (_c_int, [_vp, _vp, _vp, _c_i64, _c_i64, _c_i64, _c_i64, _c_i64,
                                           _vp, _vp, _vp, _vp]),
     "fbfp_gemv_workspace_bytes": (_c_i64, [_c_i64, _c_i64]),

@@ -126,7 +126,7 @@ template <int NT>
 __global__ void __launch_bounds__(kGemvThreads, 2)
 gemv_kernel(const GemvArgs a) {
   extern __shared__ uint4 xs[];                            // [64 kb][m][4] pieces
-  __shared__ float s_out[kGemvWarps][16][16];              // outlier partials [row][token]
+  __shared__ float s_out[kGemvWarps][16][16];              // outlier partials [token][row]
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int g = lane >> 2, t = lane & 3;
@@ -273,7 +273,7 @@ gemv_kernel(const GemvArgs a) {
         const int pos = ((e7 & 3) << 1) + (e7 >> 2);
         for (int tok = 0; tok < m; ++tok) {
           const float xv = bf16_bits_to_float(xh[x_piece_slot(kbl, tok, m, piece) * 8 + pos]);
-          atomicAdd(&s_out[warp][r][tok], v * xv);
+          atomicAdd(&s_out[warp][tok][r], v * xv);
         }
       }
     }
@@ -286,12 +286,12 @@ gemv_kernel(const GemvArgs a) {
   for (int n = 0; n < NT; ++n) {
     const int tk0 = n * 8 + 2 * t, tk1 = tk0 + 1;
     if (rv0) {
-      if (tk0 < m) red_add_f32(a.ws + (int64_t)tk0 * a.npad + row0, acc[n][0] * inv15 + s_out[warp][g][tk0]);
-      if (tk1 < m) red_add_f32(a.ws + (int64_t)tk1 * a.npad + row0, acc[n][1] * inv15 + s_out[warp][g][tk1]);
+      if (tk0 < m) red_add_f32(a.ws + (int64_t)tk0 * a.npad + row0, acc[n][0] * inv15 + s_out[warp][tk0][g]);
+      if (tk1 < m) red_add_f32(a.ws + (int64_t)tk1 * a.npad + row0, acc[n][1] * inv15 + s_out[warp][tk1][g]);
     }
     if (rv1) {
-      if (tk0 < m) red_add_f32(a.ws + (int64_t)tk0 * a.npad + row1, acc[n][2] * inv15 + s_out[warp][g + 8][tk0]);
-      if (tk1 < m) red_add_f32(a.ws + (int64_t)tk1 * a.npad + row1, acc[n][3] * inv15 + s_out[warp][g + 8][tk1]);
+      if (tk0 < m) red_add_f32(a.ws + (int64_t)tk0 * a.npad + row1, acc[n][2] * inv15 + s_out[warp][tk0][g + 8]);
+      if (tk1 < m) red_add_f32(a.ws + (int64_t)tk1 * a.npad + row1, acc[n][3] * inv15 + s_out[warp][tk1][g + 8]);
     }
   }
   __threadfence();

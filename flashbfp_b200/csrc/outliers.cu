@@ -38,10 +38,22 @@ __global__ void outlier_hist_kernel(CooView c, int64_t n_stages, int32_t* cnt) {
   }
 }
 
+// Index layout (int32 words): segment pointers [0, nseg], padded to a multiple of 4 words, then
+// per segment 68 words = 136 uint16: the start of each of the 128 rows within the segment
+// (relative to the segment start), entry 128 = the segment size, 7 words of padding.
+__host__ __device__ constexpr int64_t roff_base_words(int64_t nseg) { return (nseg + 1 + 3) & ~(int64_t)3; }
+constexpr int kRoffWords = 68;
+
 __global__ void outlier_segptr_kernel(const int32_t* dest, int64_t nseg, int32_t* seg_ptr) {
   for (int64_t s = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; s <= nseg;
        s += (int64_t)gridDim.x * blockDim.x)
     seg_ptr[s] = dest[s * kGroupRows];     // dest[nseg * 128] holds the total
+  uint16_t* roff = reinterpret_cast<uint16_t*>(seg_ptr + roff_base_words(nseg));
+  for (int64_t t = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; t < nseg * 2 * kRoffWords;
+       t += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t sgm = t / (2 * kRoffWords), r = t % (2 * kRoffWords);
+    roff[t] = r <= kGroupRows ? (uint16_t)(dest[sgm * kGroupRows + r] - dest[sgm * kGroupRows]) : (uint16_t)0;
+  }
 }
 
 __global__ void outlier_scatter_kernel(CooView c, int64_t n_stages, const int32_t* dest,
@@ -80,6 +92,13 @@ extern "C" int64_t fbfp_outlier_tiles_scratch_bytes(int64_t npad, int64_t kpad) 
   const int64_t n_groups = (npad + kGroupRows - 1) / kGroupRows;
   const int64_t n_stages = (kpad / kBlock + kStageKb - 1) / kStageKb;
   return (int64_t)(((size_t)(n_groups * n_stages * kGroupRows + 1) * sizeof(int32_t) + 255) & ~(size_t)255);
+}
+
+extern "C" int64_t fbfp_outlier_tiles_index_words(int64_t npad, int64_t kpad) {
+  const int64_t n_groups = (npad + kGroupRows - 1) / kGroupRows;
+  const int64_t n_stages = (kpad / kBlock + kStageKb - 1) / kStageKb;
+  const int64_t nseg = n_groups * n_stages;
+  return roff_base_words(nseg) + nseg * kRoffWords;
 }
 
 extern "C" int fbfp_outlier_tiles_build(const int32_t* block_idx, const int32_t* offset,

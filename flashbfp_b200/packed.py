@@ -56,10 +56,9 @@ class PackedWeight:
         L = _lib.lib()
         dev = self.device
         count = self.nnz
-        n_groups = (self.npad + 127) // 128
-        n_stages = (self.kb_row + 15) // 16
-        entries = torch.empty(max(count, 1), dtype=torch.int32, device=dev)
-        seg_ptr = torch.empty(n_groups * n_stages + 1, dtype=torch.int32, device=dev)
+        entries = torch.zeros((count + 3) // 4 * 4 + 4, dtype=torch.int32, device=dev)
+        seg_ptr = torch.empty(L.fbfp_outlier_tiles_index_words(self.npad, self.kpad), dtype=torch.int32,
+                              device=dev)
         scratch = torch.empty(L.fbfp_outlier_tiles_scratch_bytes(self.npad, self.kpad),
                               dtype=torch.uint8, device=dev)
         b, o, v = self.coo if count else (None, None, None)

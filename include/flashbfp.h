@@ -66,11 +66,16 @@ int fbfp_scatter_outliers(const int32_t* block_idx, const int32_t* offset, const
  * Replaces the (r, c, v) cache of OABFLinear.load_from_weight (triton_kernel.py:254-291).
  * Entries are grouped by (128-row group, 256-column stage); each entry is one uint32:
  * bits 0-15 fp16 value, bits 16-23 column within the stage, bits 24-30 row within the
- * group. seg_ptr has n_groups * n_stages + 1 entries (group-major), n_groups =
- * ceil(npad/128), n_stages = ceil(kpad/256); the count argument must list the COO entries
- * in ascending flat-index order, as the compressor emits them.
+ * group. `seg_ptr` (the outlier index, fbfp_outlier_tiles_index_words(npad, kpad) int32
+ * words) holds the n_groups * n_stages + 1 segment pointers (group-major; n_groups =
+ * ceil(npad/128), n_stages = ceil(kpad/256)), padded to a multiple of 4 words, followed by
+ * one 68-word block per segment: 136 uint16 row starts relative to the segment start (entry
+ * 128 = segment size). The COO list must be in ascending flat-index order, as the
+ * compressor emits it. `entries` must have room for count rounded up to a multiple of 4
+ * (the GEMV kernels copy whole 16-byte groups of it).
  * fbfp_outlier_tiles_scratch_bytes gives the scratch size the build needs.
  * ---------------------------------------------------------------------------------- */
+int64_t fbfp_outlier_tiles_index_words(int64_t npad, int64_t kpad);
 int64_t fbfp_outlier_tiles_scratch_bytes(int64_t npad, int64_t kpad);
 int fbfp_outlier_tiles_build(const int32_t* block_idx, const int32_t* offset, const uint16_t* value_f16,
                              int64_t count, int64_t kpad, int64_t npad, int64_t n_out, int64_t k_in,
