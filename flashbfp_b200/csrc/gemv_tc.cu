@@ -13,18 +13,18 @@
 //               with A read from tensor memory, one MMA per block (a small-N tcgen05.mma
 //               occupies the tensor pipe ~45 cycles whatever N <= 64, so one per block is
 //               the budget that keeps up with HBM);
-//   warps 2-3   idle (they complete the control warpgroup, which hands its registers to the
-//               dequantisers with setmaxnreg);
-//   warps 4-19  dequantisers (4 per tensor-memory lane quarter, one 4-block substage each):
+//   warps 2-3   idle;
+//   warps 4-7   epilogue (one per tensor-memory lane quarter): drain the double-buffered fp32
+//               accumulator of each (row group, CTA) segment while the next segment streams,
+//               scale by 1/15, add outlier sums, then write y or reduce across CTAs;
+//   warps 8-23  dequantisers (4 per tensor-memory lane quarter, one 4-block substage each):
 //               one row per lane; each block becomes 8 bf16 pairs s*m*2^e built
 //               exactly with bit operations (PRMT/LOP3 magic pair minus its offset, HSUB2) and
-//               stored into a tensor-memory ring with tcgen05.st; they run the epilogue
-//               (tcgen05.ld of the fp32 accumulator, 1/15 scale, red.add into the workspace;
-//               the last CTA of a row group adds bias and writes y);
+//               stored into a tensor-memory ring with tcgen05.st;
 //               outliers ride along: the producer stages each stage's outlier entries and
-//               per-row starts, and each dequantiser accumulates v * x in fp32 for the row's
-//               outliers and its own 4 tokens (x read from the stage's activation tile), added
-//               to the accumulator in the epilogue.
+//               per-row starts, and the dequantisers accumulate v * x in fp32 for the row's
+//               outliers (x read from the stage's activation tile; for M <= 4 the 4 warps of
+//               a row split its entries) and hand the sums to the epilogue through shared memory.
 // Work: stream-K over units (128-row group, 16-block stage); each CTA takes a contiguous
 // range. Every mbarrier wait is bounded: on timeout the CTA records an error code in the
 // workspace and winds down (waiting, bounded, for its own copies) before freeing TMEM.
@@ -43,30 +43,32 @@ constexpr int kASlots = 12;                     // tensor-memory A ring (4 block
 constexpr int kPayOff = 0;                      // 128 rows x 128 B, 128-byte swizzle
 constexpr int kSgnOff = 128 * 128;              // 128 rows x 32 B
 constexpr int kExpOff = kSgnOff + 128 * 32;     // 128 rows x 16 B
-constexpr int kXOff = kExpOff + 128 * 16;       // 16 blocks x (2 k-groups x 16 tokens x 16 B)
-constexpr int kXPerKb = 512;
-constexpr int kOutOff = kXOff + kStageKb * kXPerKb;           // stage's outlier entries
+constexpr int kXOff = kExpOff + 128 * 16;       // activations: 4 boxes of 64 k x <= 16 tokens
+constexpr int kXBox = 2048;                     // (128-byte swizzled rows, two 1024-byte atoms)
+constexpr int kOutOff = kXOff + 4 * kXBox;                    // stage's outlier entries
 constexpr int kOutCap = 2048;                                 // entries staged per stage
 constexpr int kRoffOff = kOutOff + kOutCap * 4;              // 136 uint16 row starts of the stage
 constexpr int kRoffBytes = 272;
 constexpr int kStageBytes = kRoffOff + 1024;                  // 39936 (multiple of 1024)
-constexpr uint32_t kDenseTx = kOutOff;                        // bytes of the four tensor copies
+constexpr uint32_t kWeightTx = kXOff;                        // payload + signs + exponents bytes
 constexpr int kSegCache = 1024;                               // segment pointers cached per CTA
-constexpr int kDq = 16;                         // dequantiser warps (2..17), 4 per lane quarter
-constexpr int kThreads = 32 * (4 + kDq);         // control warpgroup + dequantisers
-// Register split: the block launches with kRegsLaunch per thread (5 warps per SM sub-partition
-// fit its 16K registers only below ~102); the control warpgroup then drops to kRegsCtl and the
-// dequantiser warpgroups rise to kRegsDq, drawing exactly on what the control warps released.
-constexpr int kRegsLaunch = 96, kRegsCtl = 48, kRegsDq = 104;
-static_assert(4 * 32 * kRegsCtl + kDq * 32 * kRegsDq <= kThreads * kRegsLaunch, "register split");
+constexpr int kDq = 16;
+static_assert(kASlots % 4 == 0, "each dequantiser warp owns every 4th A slot");                         // dequantiser warps (2..17), 4 per lane quarter
+constexpr int kEpiWarp0 = 4;                    // epilogue warpgroup: warps 4-7
+constexpr int kDqWarp0 = 8;                     // dequantisers: warps 8 .. 8 + kDq - 1
+constexpr int kThreads = 32 * (kDqWarp0 + kDq); // 768: 6 warps per SM sub-partition at 80 registers
 static_assert(kDq % 4 == 0, "dequantisers come in whole warpgroups");
 constexpr uint32_t kTmemCols = 512;
 constexpr uint32_t kTmemD = 0;                  // 2 accumulators x 16 columns
 constexpr uint32_t kTmemA = 32;                 // 12 slots x 32 columns (4 blocks x 8)
 constexpr size_t kSoutOff = (size_t)kStages * kStageBytes;
 constexpr size_t kSegOff = kSoutOff;
-constexpr size_t kBarOff = kSegOff + (kSegCache + 8) * sizeof(int32_t);
-constexpr int kNumBars = 2 * kStages + 2 * kASlots + 4 + 1;
+// outlier partial sums handed from dequantisers to the epilogue: [2 accumulators][4 warps of a
+// row][4 tokens][128 rows] fp32
+constexpr size_t kOaccOff = kSegOff + (kSegCache + 8) * sizeof(int32_t);
+constexpr size_t kOaccBytes = 2 * 4 * 4 * 128 * sizeof(float);
+constexpr size_t kBarOff = kOaccOff + kOaccBytes;
+constexpr int kNumBars = 2 * kStages + 2 * kASlots + 8;
 constexpr size_t kSmemBytes = kBarOff + kNumBars * 8 + 16 + 1024;   // + alignment slack
 }  // namespace tc
 
@@ -78,10 +80,10 @@ struct TcShared {
   uint8_t* stage;
   float* s_out;
   int32_t* seg;          // seg_ptr[u0 .. u0 + kSegCache]
-  uint64_t *full, *empty, *afull, *aempty, *dfull, *dempty, *dqsync;
+  uint64_t *full, *empty, *afull, *aempty, *dfull, *dempty, *ofull, *oempty;
+  float* oacc;           // [2][4][4][128]
   uint32_t* tmem_slot;
   volatile int* abort_flag;
-  int* last_flag;
 };
 
 __device__ __forceinline__ TcShared tc_shared(uint8_t* smem_raw) {
@@ -98,10 +100,11 @@ __device__ __forceinline__ TcShared tc_shared(uint8_t* smem_raw) {
   S.aempty = S.afull + tc::kASlots;
   S.dfull = S.aempty + tc::kASlots;
   S.dempty = S.dfull + 2;
-  S.dqsync = S.dempty + 2;
-  S.tmem_slot = reinterpret_cast<uint32_t*>(S.dqsync + 1);
+  S.ofull = S.dempty + 2;
+  S.oempty = S.ofull + 2;
+  S.oacc = reinterpret_cast<float*>(smem + tc::kOaccOff);
+  S.tmem_slot = reinterpret_cast<uint32_t*>(S.oempty + 2);
   S.abort_flag = reinterpret_cast<volatile int*>(S.tmem_slot + 1);
-  S.last_flag = reinterpret_cast<int*>(S.tmem_slot + 2);
   return S;
 }
 
@@ -118,16 +121,6 @@ __device__ __forceinline__ bool tc_wait(const TcShared& S, const TcArgs& a, uint
   *S.abort_flag = 1;
   atomicExch(a.err, code);
   return false;
-}
-
-// Barrier among the dequantiser warps (lane 0 of each arrives), bounded.
-__device__ __forceinline__ bool dq_sync(const TcShared& S, const TcArgs& a, uint32_t& uses) {
-  __syncwarp();
-  if ((threadIdx.x & 31) == 0) mbar_arrive(S.dqsync);
-  const bool ok = tc_wait(S, a, S.dqsync, uses & 1, 9);
-  ++uses;
-  __syncwarp();
-  return ok;
 }
 
 // Outlier-entry range of local unit i (global unit u0 + i): [lo, hi) plus the 16-byte aligned
@@ -156,20 +149,26 @@ __device__ void tc_producer(const TcShared& S, const TcArgs& a, const TcMaps& M,
   int64_t i = 0;
   if (elect_one_sync()) {
     prefetch_tmap(&M.pay); prefetch_tmap(&M.sgn); prefetch_tmap(&M.exp); prefetch_tmap(&M.x);
+    int s = 0;
+    uint32_t ph = 0;
+    int rg = (int)(u0 / a.n_stages), st = (int)(u0 % a.n_stages);
+    const uint32_t xbytes = 4u * 128u * (uint32_t)a.m;          // 4 boxes of 64 k x m tokens
     for (int64_t u = u0; u < u1; ++u, ++i) {
-      const int s = (int)(i % tc::kStages);
-      const uint32_t use = (uint32_t)(i / tc::kStages);
-      if (!tc_wait(S, a, &S.empty[s], (use & 1) ^ 1, 1)) break;
-      const int rg = (int)(u / a.n_stages), st = (int)(u % a.n_stages);
+      if (!tc_wait(S, a, &S.empty[s], ph ^ 1, 1)) break;
       uint8_t* sb = S.stage + (size_t)s * tc::kStageBytes;
       const OutRange orr = out_range(S, a, u0, i);
-      mbar_arrive_expect_tx(&S.full[s], tc::kDenseTx + (uint32_t)orr.n * 4 + (a.entries ? tc::kRoffBytes : 0));
+      mbar_arrive_expect_tx(&S.full[s], tc::kWeightTx + xbytes + (uint32_t)orr.n * 4 +
+                                            (a.entries ? tc::kRoffBytes : 0));
       tma_2d_g2s(sb + tc::kPayOff, &M.pay, st * 128, rg * 128, &S.full[s]);
       tma_2d_g2s(sb + tc::kSgnOff, &M.sgn, st * kStageKb, rg * 128, &S.full[s]);
       tma_2d_g2s(sb + tc::kExpOff, &M.exp, st * kStageKb, rg * 128, &S.full[s]);
-      tma_3d_g2s(sb + tc::kXOff, &M.x, 0, 0, st * 2 * kStageKb, &S.full[s]);
+#pragma unroll
+      for (int b = 0; b < 4; ++b)
+        tma_2d_g2s(sb + tc::kXOff + b * tc::kXBox, &M.x, st * 256 + b * 64, 0, &S.full[s]);
       if (orr.n) bulk_g2s(sb + tc::kOutOff, a.entries + orr.lo4, (uint32_t)orr.n * 4, &S.full[s]);
       if (a.entries) bulk_g2s(sb + tc::kRoffOff, roff_block(a, u), tc::kRoffBytes, &S.full[s]);
+      if (++s == tc::kStages) { s = 0; ph ^= 1; }
+      if (++st == a.n_stages) { st = 0; ++rg; }
     }
     // wind down: every stage issued so far must have landed before the CTA may exit
     for (int64_t j = i > tc::kStages ? i - tc::kStages : 0; j < i; ++j)
@@ -181,12 +180,15 @@ __device__ void tc_producer(const TcShared& S, const TcArgs& a, const TcMaps& M,
 // ---------------------------------------------------------------------------------------
 __device__ void tc_mma(const TcShared& S, const TcArgs& a, int64_t u0, int64_t u1, uint32_t tmem) {
   constexpr uint32_t IDESC = idesc_bf16_f32(128, 16, false);
-  // B tile of one block: [k-group 2][16 tokens][8 bf16]: LBO 256 B (K), SBO 128 B (N); the tiles of
-  // consecutive blocks are 512 B apart, i.e. +32 in the descriptor's address field
-  const uint64_t desc0 = smem_desc_noswizzle(smem_u32(S.stage + tc::kXOff), 256, 128);
+  // B: a substage's 4 blocks are one 64-k box of tokens (rows) in 128-byte swizzled K-major
+  // layout; token groups of 8 are 1024 B apart; block j of the box starts 32 * j bytes in
+  const uint64_t desc0 = smem_desc_sw128(smem_u32(S.stage + tc::kXOff), 1024);
   constexpr uint64_t kStageDesc = (uint64_t)(tc::kStageBytes >> 4);
-  constexpr uint64_t kKbDesc = (uint64_t)(tc::kXPerKb >> 4);
-  int64_t i = 0, jsub = 0, seg = 0;
+  constexpr uint64_t kBoxDesc = (uint64_t)(tc::kXBox >> 4);
+  constexpr uint64_t kKbDesc = 2;                                 // 32 bytes
+  int64_t seg = 0;
+  int s = 0, slot = 0;
+  uint32_t aph = 0;
   for (int64_t u = u0; u < u1; ++seg) {
     const int64_t rg = u / a.n_stages;
     const int64_t seg_end = min(u1, (rg + 1) * a.n_stages);
@@ -195,23 +197,23 @@ __device__ void tc_mma(const TcShared& S, const TcArgs& a, int64_t u0, int64_t u
     tc_fence_after();
     const uint32_t tD = tmem + tc::kTmemD + d * 16;
     uint32_t acc = 0;
-    for (; u < seg_end; ++u, ++i) {
-      const int s = (int)(i % tc::kStages);
+    for (; u < seg_end; ++u) {
       const uint64_t dstage = desc0 + (uint64_t)s * kStageDesc;
-      for (int sub = 0; sub < 4; ++sub, ++jsub) {
-        const int slot = (int)(jsub % tc::kASlots);
-        if (!tc_wait(S, a, &S.afull[slot], (uint32_t)(jsub / tc::kASlots) & 1, 3)) return;
+      for (int sub = 0; sub < 4; ++sub) {
+        if (!tc_wait(S, a, &S.afull[slot], aph, 3)) return;
         tc_fence_after();
         const uint32_t tA = tmem + tc::kTmemA + slot * 32;
-        const uint64_t dsub = dstage + (uint64_t)(sub * 4) * kKbDesc;
+        const uint64_t dsub = dstage + (uint64_t)sub * kBoxDesc;
         mma_ts(tD, tA + 0, dsub + 0 * kKbDesc, IDESC, acc);
         mma_ts(tD, tA + 8, dsub + 1 * kKbDesc, IDESC, 1);
         mma_ts(tD, tA + 16, dsub + 2 * kKbDesc, IDESC, 1);
         mma_ts(tD, tA + 24, dsub + 3 * kKbDesc, IDESC, 1);
         acc = 1;
         mma_commit(&S.aempty[slot]);
+        if (++slot == tc::kASlots) { slot = 0; aph ^= 1; }
       }
       mma_commit(&S.empty[s]);
+      if (++s == tc::kStages) s = 0;
     }
     mma_commit(&S.dfull[d]);
   }
@@ -222,7 +224,7 @@ __device__ void tc_mma(const TcShared& S, const TcArgs& a, int64_t u0, int64_t u
 // v = +-(128 + m) * 2^e (sign bit 15/31, exponent field e + 134, nibble in bits 0-3/16-19) and
 // c = +-128 * 2^e are built with bit operations; v - c is exact in bf16.
 __device__ __forceinline__ void dq_block(uint32_t w0, uint32_t w1, uint32_t s16, uint32_t eb,
-                                         uint32_t* out) {
+                                         uint32_t (&out)[8]) {
   const uint32_t SM = 0x80008000u, NM = 0x000F000Fu;
   const uint32_t y = s16 | (s16 << 15);          // sign bit b lands on 15 and 31 after << (15 - b)
   const uint32_t K = eb * 0x00800080u;
@@ -243,130 +245,205 @@ __device__ __forceinline__ void dq_block(uint32_t w0, uint32_t w1, uint32_t s16,
   }
 }
 
-// Segment-end synchronisation and epilogue shared by dequantisers (and, for the barrier
-// points, the outlier warps).
+// Outliers of row lr in one stage (their dense slots are +0): oacc[t] += v * x[otok + t] for
+// NT tokens over the row's entries first, first + step, ...; x comes from the stage's activation
+// tile: column c of token t is in box c / 64, 1024-byte atom t / 8, 128-byte row t % 8, 16-byte
+// chunk ((c % 64) / 8) ^ (t % 8) (128-byte swizzle), element c % 8.
+template <int NT>
+__device__ __forceinline__ void tc_row_outliers(const uint8_t* sb, const OutRange& orr,
+                                                const uint32_t* entries, int lr, int first, int step,
+                                                int otok, float* oacc) {
+  const uint16_t* ro = reinterpret_cast<const uint16_t*>(sb + tc::kRoffOff);
+  const uint32_t* es = reinterpret_cast<const uint32_t*>(sb + tc::kOutOff);
+  const uint8_t* xs = sb + tc::kXOff + (otok >> 3) * 1024;
+  const int e_end = ro[lr + 1];
+  const int obase = orr.lo - orr.lo4;
+  for (int t = ro[lr] + first; t < e_end; t += step) {
+    const int o = obase + t;
+    const uint32_t e = o < orr.n ? es[o] : __ldg(entries + orr.lo + t);
+    const float v = __half2float(__ushort_as_half((unsigned short)(e & 0xFFFFu)));
+    // box * 2048 + (c % 8) * 2 from bits 22-23 and 16-18 of the entry; chunk from bits 19-21
+    const uint8_t* xp = xs + (((e >> 11) & 0x1800u) | ((e >> 15) & 0xEu));
+    const uint32_t chunk = (e >> 19) & 7u;
+#pragma unroll
+    for (int tt = 0; tt < NT; ++tt) {
+      const uint32_t r = (uint32_t)((otok + tt) & 7);
+      const uint32_t off = (r << 7) | ((chunk ^ r) << 4);
+      oacc[tt] = fmaf(v, __uint_as_float((uint32_t)*reinterpret_cast<const uint16_t*>(xp + off) << 16),
+                      oacc[tt]);
+    }
+  }
+}
+
+// Dequantisers: dense blocks into the tensor-memory A ring, outliers, segment epilogue.
 __device__ void tc_dequant(const TcShared& S, const TcArgs& a, int64_t u0, int64_t u1, uint32_t tmem) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int wi = warp - 4;                 // 0..kDq-1
+  const int wi = warp - tc::kDqWarp0;     // 0..kDq-1
   const int q4 = warp & 3;                 // tensor-memory lane quarter
   const int par = wi >> 2;                 // which of the 4 substages of a stage (and token quarter)
   const int lr = q4 * 32 + lane;           // row within the group
   const uint32_t lane_base = (uint32_t)(q4 * 32) << 16;
   const int sw = lr & 7;                   // 128-byte swizzle phase of this row
   const int m = a.m;
-  uint32_t sync_uses = 0;
+  // Outliers: with m <= 4 the 4 warps sharing a row split its entries (every 4th) and each
+  // accumulates tokens 0..3; with more tokens each warp takes all entries for its own 4 tokens.
+  const bool split = m <= 4;
+  const int otok = split ? 0 : par * 4;          // first token of oacc
+  const int ofirst = split ? par : 0, ostep = split ? 4 : 1;
+  const bool do_out_warp = a.entries != nullptr && otok < m;
   int64_t i = 0, seg = 0;
+  int s = 0, ai = 0;                      // stage ring slot; this warp's A slot is 4 * ai + par
+  uint32_t sph = 0, aph = 0;
   for (int64_t u = u0; u < u1; ++seg) {
     const int64_t rg = u / a.n_stages;
-    const int64_t seg_begin = u, seg_end = min(u1, (rg + 1) * a.n_stages);
+    const int64_t seg_end = min(u1, (rg + 1) * a.n_stages);
     const int64_t row = rg * 128 + lr;
     const bool rvalid = row < a.npad;
-    const bool do_out = a.entries && rvalid && par * 4 < m;
     float oacc[4] = {0.f, 0.f, 0.f, 0.f};
     for (; u < seg_end; ++u, ++i) {
-      const int s = (int)(i % tc::kStages);
-      if (!tc_wait(S, a, &S.full[s], (uint32_t)(i / tc::kStages) & 1, 4)) return;
+      if (!tc_wait(S, a, &S.full[s], sph, 4)) return;
       const uint8_t* sb = S.stage + (size_t)s * tc::kStageBytes;
       {
         const int sub = par;
-        const int64_t j = 4 * i + sub;
-        const int slot = (int)(j % tc::kASlots);
+        const int slot = 4 * ai + par;
+        // the A slot is normally free already (the ring runs 3 stages ahead of the MMA)
+        if (!tc_wait(S, a, &S.aempty[slot], aph ^ 1, 5)) return;
+        tc_fence_after();
         const uint8_t* prow = sb + tc::kPayOff + lr * 128;
         const uint4 P0 = *reinterpret_cast<const uint4*>(prow + (((2 * sub) ^ sw) << 4));
         const uint4 P1 = *reinterpret_cast<const uint4*>(prow + (((2 * sub + 1) ^ sw) << 4));
         const uint2 SG = *reinterpret_cast<const uint2*>(sb + tc::kSgnOff + lr * 32 + sub * 8);
         const uint32_t EX = *reinterpret_cast<const uint32_t*>(sb + tc::kExpOff + lr * 16 + sub * 4);
         const uint32_t E = (EX ^ 0x80808080u) + 0x06060606u;     // e + 134 per byte
-        uint32_t w[32];
-        dq_block(P0.x, P0.y, SG.x & 0xFFFFu, E & 0xFFu, w + 0);
-        dq_block(P0.z, P0.w, SG.x >> 16, (E >> 8) & 0xFFu, w + 8);
-        dq_block(P1.x, P1.y, SG.y & 0xFFFFu, (E >> 16) & 0xFFu, w + 16);
-        dq_block(P1.z, P1.w, SG.y >> 16, E >> 24, w + 24);
-        if (!rvalid) {                                          // rows past npad (TMA zero fill)
-#pragma unroll
-          for (int r = 0; r < 32; ++r) w[r] = 0u;
-        }
-        if (!tc_wait(S, a, &S.aempty[slot], ((uint32_t)(j / tc::kASlots) & 1) ^ 1, 5)) return;
-        tc_fence_after();
-        tmem_st_32x32b_x32(tmem + tc::kTmemA + slot * 32 + lane_base, w);
+        // rows past npad arrive as zero bytes (TMA fill) and dequantise to +0
+        const uint32_t ta = tmem + tc::kTmemA + slot * 32 + lane_base;
+        uint32_t w[8];
+        dq_block(P0.x, P0.y, SG.x & 0xFFFFu, E & 0xFFu, w);
+        tmem_st_32x32b_x8(ta + 0, w);
+        dq_block(P0.z, P0.w, SG.x >> 16, (E >> 8) & 0xFFu, w);
+        tmem_st_32x32b_x8(ta + 8, w);
+        dq_block(P1.x, P1.y, SG.y & 0xFFFFu, (E >> 16) & 0xFFu, w);
+        tmem_st_32x32b_x8(ta + 16, w);
+        dq_block(P1.z, P1.w, SG.y >> 16, E >> 24, w);
+        tmem_st_32x32b_x8(ta + 24, w);
         tmem_wait_st();
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(&S.afull[slot]);
       }
-      if (do_out) {
-        // outliers of this row in this stage (their dense slots are +0): acc += v * x for the
-        // warp's 4 tokens, x read from the stage's activation tile [k-group][16 tokens][8]
+      if (do_out_warp) {
         const OutRange orr = out_range(S, a, u0, i);
-        const uint16_t* ro = reinterpret_cast<const uint16_t*>(sb + tc::kRoffOff);
-        const uint32_t* es = reinterpret_cast<const uint32_t*>(sb + tc::kOutOff);
-        const uint8_t* xs = sb + tc::kXOff + par * 4 * 16;
-        const int e_end = ro[lr + 1];
-        for (int t = ro[lr]; t < e_end; ++t) {
-          const int o = orr.lo + t - orr.lo4;
-          const uint32_t e = o < orr.n ? es[o] : __ldg(a.entries + orr.lo + t);
-          const uint32_t c = (e >> 16) & 0xFFu;
-          const float v = __half2float(__ushort_as_half((unsigned short)(e & 0xFFFFu)));
-          const uint8_t* xp = xs + (c >> 4) * tc::kXPerKb + ((c >> 3) & 1) * 256 + (c & 7) * 2;
-#pragma unroll
-          for (int tt = 0; tt < 4; ++tt)
-            oacc[tt] = fmaf(v, __uint_as_float((uint32_t)*reinterpret_cast<const uint16_t*>(xp + tt * 16) << 16),
-                            oacc[tt]);
+        if (rvalid) {
+          if (m == 1) tc_row_outliers<1>(sb, orr, a.entries, lr, ofirst, ostep, otok, oacc);
+          else tc_row_outliers<4>(sb, orr, a.entries, lr, ofirst, ostep, otok, oacc);
         }
       }
       __syncwarp();
       if (lane == 0) mbar_arrive(&S.empty[s]);
+      if (++s == tc::kStages) { s = 0; sph ^= 1; }
+      if (++ai == tc::kASlots / 4) { ai = 0; aph ^= 1; }
     }
 
-    // ---- segment epilogue ----
+    // ---- segment end: hand the outlier partial sums to the epilogue warps ----
+    if (a.entries) {
+      const int d = (int)(seg & 1);
+      if (!tc_wait(S, a, &S.oempty[d], ((uint32_t)(seg >> 1) & 1) ^ 1, 7)) return;
+      float* so = S.oacc + (size_t)((d * 4 + par) * 4) * 128 + lr;
+#pragma unroll
+      for (int t = 0; t < 4; ++t) so[t * 128] = oacc[t];
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&S.ofull[d]);
+    }
+  }
+}
+
+// Epilogue warpgroup (warp w reads tensor-memory lane quarter w % 4, i.e. rows 32q .. 32q+31 of
+// the group): per segment it drains the accumulator (all m tokens), adds the dequantisers'
+// outlier partial sums, then either writes y directly (the CTA covered the whole row group) or
+// adds into the fp32 workspace; a counter per (row group, quarter) collects the units of all
+// CTAs and the warp that completes it writes y and returns the workspace rows to zero.
+__device__ void tc_epilogue(const TcShared& S, const TcArgs& a, int64_t u0, int64_t u1, uint32_t tmem) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int q4 = warp & 3;
+  const int lr = q4 * 32 + lane;
+  const uint32_t lane_base = (uint32_t)(q4 * 32) << 16;
+  const int m = a.m;
+  const bool split = m <= 4;
+  const float inv15 = 1.0f / 15.0f;
+  int64_t seg = 0;
+  for (int64_t u = u0; u < u1; ++seg) {
+    const int64_t rg = u / a.n_stages;
+    const int64_t seg_begin = u, seg_end = min(u1, (rg + 1) * a.n_stages);
+    u = seg_end;
+    const int64_t row = rg * 128 + lr;
+    const bool rvalid = row < a.npad;
     const int d = (int)(seg & 1);
-    if (!tc_wait(S, a, &S.dfull[d], (uint32_t)(seg >> 1) & 1, 6)) return;
+    const uint32_t ph = (uint32_t)(seg >> 1) & 1;
+    if (!tc_wait(S, a, &S.dfull[d], ph, 6)) return;
     tc_fence_after();
-    float dv[4];
-    tmem_ld_32x32b_x4(tmem + tc::kTmemD + d * 16 + par * 4 + lane_base, dv);
+    float val[16];
+    tmem_ld_32x32b_x16(tmem + tc::kTmemD + d * 16 + lane_base, val);
     tmem_wait_ld();
     tc_fence_before();
     __syncwarp();
     if (lane == 0) mbar_arrive(&S.dempty[d]);
-    const float inv15 = 1.0f / 15.0f;
 #pragma unroll
-    for (int t = 0; t < 4; ++t) {
-      const int tok = par * 4 + t;
-      if (tok < m && rvalid) {
-        asm volatile("red.global.add.f32 [%0], %1;\n" ::"l"(a.ws + (int64_t)tok * a.npad + row),
-                     "f"(fmaf(dv[t], inv15, oacc[t])) : "memory");
+    for (int t = 0; t < 16; ++t) val[t] *= inv15;
+    if (a.entries) {
+      if (!tc_wait(S, a, &S.ofull[d], ph, 8)) return;
+      const float* so = S.oacc + (size_t)(d * 16) * 128 + lr;      // [par][t][row]
+      if (split) {
+#pragma unroll
+        for (int t = 0; t < 4; ++t)
+          val[t] += (so[t * 128] + so[(4 + t) * 128]) + (so[(8 + t) * 128] + so[(12 + t) * 128]);
+      } else {
+#pragma unroll
+        for (int t = 0; t < 16; ++t) val[t] += so[t * 128];
       }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&S.oempty[d]);
+    }
+    const bool whole = seg_begin == rg * a.n_stages && seg_end == (rg + 1) * a.n_stages;
+    if (whole) {
+      if (rvalid && row < a.n_out) {
+        const float bv = a.bias ? load_as_float(a.bias, a.bias_dtype, row) : 0.f;
+#pragma unroll
+        for (int t = 0; t < 16; ++t)
+          if (t < m) store_from_float(a.y, a.y_dtype, (int64_t)t * a.ldy + row, val[t] + bv);
+      }
+      continue;
+    }
+    if (rvalid) {
+#pragma unroll
+      for (int t = 0; t < 16; ++t)
+        if (t < m)
+          asm volatile("red.global.add.f32 [%0], %1;\n" ::"l"(a.ws + (int64_t)t * a.npad + row),
+                       "f"(val[t]) : "memory");
     }
     __threadfence();
-    if (!dq_sync(S, a, sync_uses)) return;
-    if (wi == 0 && lane == 0) {
+    __syncwarp();
+    const int units = (int)(seg_end - seg_begin);
+    int old = 0;
+    if (lane == 0) old = atomicAdd(a.counters + rg * 4 + q4, units);
+    old = __shfl_sync(0xffffffffu, old, 0);
+    if (old + units == a.n_stages) {
       __threadfence();
-      const int units = (int)(seg_end - seg_begin);
-      const int old = atomicAdd(a.counters + rg, units);
-      *S.last_flag = (old + units == a.n_stages);
-    }
-    if (!dq_sync(S, a, sync_uses)) return;
-    if (*S.last_flag) {
-      __threadfence();
-      for (int p = wi * 32 + lane; p < 128 * m; p += 32 * tc::kDq) {
-        const int tok = p >> 7, r = p & 127;
-        const int64_t rw = rg * 128 + r;
-        if (rw >= a.npad) continue;
-        float* wp = a.ws + (int64_t)tok * a.npad + rw;
-        float val = __ldcg(wp);
-        __stcg(wp, 0.f);
-        if (rw < a.n_out) {
-          if (a.bias) val += load_as_float(a.bias, a.bias_dtype, rw);
-          store_from_float(a.y, a.y_dtype, (int64_t)tok * a.ldy + rw, val);
+      if (rvalid) {
+        const float bv = (a.bias && row < a.n_out) ? load_as_float(a.bias, a.bias_dtype, row) : 0.f;
+        for (int t = 0; t < m; ++t) {
+          float* wp = a.ws + (int64_t)t * a.npad + row;
+          const float v = __ldcg(wp);
+          __stcg(wp, 0.f);
+          if (row < a.n_out) store_from_float(a.y, a.y_dtype, (int64_t)t * a.ldy + row, v + bv);
         }
       }
-      if (wi == 0 && lane == 0) a.counters[rg] = 0;
+      __syncwarp();
+      if (lane == 0) a.counters[rg * 4 + q4] = 0;
     }
-    if (!dq_sync(S, a, sync_uses)) return;
   }
 }
 
-__global__ void __maxnreg__(tc::kRegsLaunch)
+__global__ void __launch_bounds__(tc::kThreads, 1)
 gemv_tc_kernel(const TcArgs a, const __grid_constant__ TcMaps M) {
   extern __shared__ uint8_t smem_raw[];
   const TcShared S = tc_shared(smem_raw);
@@ -378,10 +455,13 @@ gemv_tc_kernel(const TcArgs a, const __grid_constant__ TcMaps M) {
   if (threadIdx.x == 0) {
     for (int s = 0; s < tc::kStages; ++s) { mbar_init(&S.full[s], 1); mbar_init(&S.empty[s], tc::kDq + 1); }
     for (int j = 0; j < tc::kASlots; ++j) { mbar_init(&S.afull[j], 4); mbar_init(&S.aempty[j], 1); }
-    for (int d = 0; d < 2; ++d) { mbar_init(&S.dfull[d], 1); mbar_init(&S.dempty[d], tc::kDq); }
-    mbar_init(S.dqsync, tc::kDq);
+    for (int d = 0; d < 2; ++d) {
+      mbar_init(&S.dfull[d], 1);
+      mbar_init(&S.dempty[d], 4);                 // the 4 epilogue warps
+      mbar_init(&S.ofull[d], tc::kDq);
+      mbar_init(&S.oempty[d], 4);
+    }
     *S.abort_flag = 0;
-    *S.last_flag = 0;
     fence_mbar_init();
   }
   if (a.entries) {
@@ -397,16 +477,14 @@ gemv_tc_kernel(const TcArgs a, const __grid_constant__ TcMaps M) {
   tc_fence_after();
   const uint32_t tmem = *S.tmem_slot;
 
-  if (warp < 4) {
-    regs_release<tc::kRegsCtl>();
-    if (warp == 0) {
-      tc_producer(S, a, M, u0, u1);
-    } else if (warp == 1) {
-      if (elect_one_sync()) tc_mma(S, a, u0, u1, tmem);
-      __syncwarp();
-    }
-  } else {
-    regs_acquire<tc::kRegsDq>();
+  if (warp == 0) {
+    tc_producer(S, a, M, u0, u1);
+  } else if (warp == 1) {
+    if (elect_one_sync()) tc_mma(S, a, u0, u1, tmem);
+    __syncwarp();
+  } else if (warp >= tc::kEpiWarp0 && warp < tc::kDqWarp0) {
+    tc_epilogue(S, a, u0, u1, tmem);
+  } else if (warp >= tc::kDqWarp0) {
     tc_dequant(S, a, u0, u1, tmem);
   }
 
@@ -465,18 +543,18 @@ static int encode_2d(CUtensorMap* m, CUtensorMapDataType dt, const void* base, u
   return FBFP_OK;
 }
 
-// Activations X[m][k] (bf16, leading dim ldx) as a 3-D tensor (8 elements, token, k-group)
-// so that one copy lands a stage directly in the MMA's K-major core-matrix layout
-// [k-group][16 tokens][8 elements]; tokens >= m and columns >= k_in are zero-filled.
+// Activations X[m][k] (bf16, leading dim ldx) as a 2-D tensor (k, token) copied in boxes of
+// 64 k x m tokens with 128-byte swizzle: each box lands as the MMA's K-major B operand for
+// 4 blocks (token rows 8 and up in the second 1024-byte atom); columns >= k_in are zero-filled.
 static int encode_x(CUtensorMap* m, const void* x, int64_t tokens, int64_t k_in, int64_t ldx) {
   EncodeTiledFn fn = encode_fn();
   if (!fn) return set_error(FBFP_ERR_CUDA, "cuTensorMapEncodeTiled is not available");
-  const cuuint64_t dims[3] = {8, (cuuint64_t)tokens, (cuuint64_t)(k_in / 8)};
-  const cuuint64_t strides[2] = {(cuuint64_t)ldx * 2, 16};
-  const cuuint32_t box[3] = {8, 16, 2 * kStageKb};
-  const cuuint32_t es[3] = {1, 1, 1};
-  CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(x), dims, strides, box, es,
-                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+  const cuuint64_t dims[2] = {(cuuint64_t)k_in, (cuuint64_t)tokens};
+  const cuuint64_t strides[1] = {(cuuint64_t)ldx * 2};
+  const cuuint32_t box[2] = {64, (cuuint32_t)tokens};
+  const cuuint32_t es[2] = {1, 1};
+  CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(x), dims, strides, box, es,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
                   CU_TENSOR_MAP_L2_PROMOTION_L2_128B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) return set_error(FBFP_ERR_CUDA, "cuTensorMapEncodeTiled(x) failed (%d)", (int)r);
   return FBFP_OK;
