@@ -308,7 +308,7 @@ def run_ours(args):
             "decode_tokens_per_s_note": "linear layers only (no attention/norm/lm_head)",
             "layers_gbs_per_rank": {kk: round(v, 1) for kk, v in per_rank_kind.items()},
             "roofline": {
-                "bound": "hbm", "kernel": "gemv_kernel (gate|up 30720x3840 launches)",
+                "bound": "hbm", "kernel": "gemv_tc_kernel (gate|up 30720x3840 launches)",
                 "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                 "frac": round(achieved / peak, 4), "peak_source": peaks["source"],
                 "traffic": _traffic(m),
