@@ -33,6 +33,8 @@
 #include "common.cuh"
 #include "sm100.cuh"
 #include "tc_args.h"
+#include "tc_host.h"
+#include "dq_pair.cuh"
 
 namespace fbfp {
 using namespace sm100;
@@ -219,32 +221,6 @@ __device__ void tc_mma(const TcShared& S, const TcArgs& a, int64_t u0, int64_t u
   }
 }
 
-// ---------------------------------------------------------------------------------------
-// One block -> 8 bf16 pairs of natural elements (2j, 2j+1), each element exactly s*m*2^e:
-// v = +-(128 + m) * 2^e (sign bit 15/31, exponent field e + 134, nibble in bits 0-3/16-19) and
-// c = +-128 * 2^e are built with bit operations; v - c is exact in bf16.
-__device__ __forceinline__ void dq_block(uint32_t w0, uint32_t w1, uint32_t s16, uint32_t eb,
-                                         uint32_t (&out)[8]) {
-  const uint32_t SM = 0x80008000u, NM = 0x000F000Fu;
-  const uint32_t y = s16 | (s16 << 15);          // sign bit b lands on 15 and 31 after << (15 - b)
-  const uint32_t K = eb * 0x00800080u;
-  const uint32_t t0 = w0 >> 4, t1 = w1 >> 4;
-#pragma unroll
-  for (int j = 0; j < 4; ++j) {
-    const uint32_t sel = (uint32_t)j | ((uint32_t)(4 + j) << 8);   // byte j of w, byte j of w>>4
-    const uint32_t c0 = ((y << (15 - 2 * j)) & SM) | K;
-    const uint32_t c1 = ((y << (7 - 2 * j)) & SM) | K;
-    const uint32_t v0 = (__byte_perm(w0, t0, sel) & NM) | c0;
-    const uint32_t v1 = (__byte_perm(w1, t1, sel) & NM) | c1;
-    __nv_bfloat162 r0 = __hsub2(*reinterpret_cast<const __nv_bfloat162*>(&v0),
-                                *reinterpret_cast<const __nv_bfloat162*>(&c0));
-    __nv_bfloat162 r1 = __hsub2(*reinterpret_cast<const __nv_bfloat162*>(&v1),
-                                *reinterpret_cast<const __nv_bfloat162*>(&c1));
-    out[j] = *reinterpret_cast<uint32_t*>(&r0);
-    out[4 + j] = *reinterpret_cast<uint32_t*>(&r1);
-  }
-}
-
 // Outliers of row lr in one stage (their dense slots are +0): oacc[t] += v * x[otok + t] for
 // NT tokens over the row's entries first, first + step, ...; x comes from the stage's activation
 // tile: column c of token t is in box c / 64, 1024-byte atom t / 8, 128-byte row t % 8, 16-byte
@@ -285,11 +261,12 @@ __device__ void tc_dequant(const TcShared& S, const TcArgs& a, int64_t u0, int64
   const uint32_t lane_base = (uint32_t)(q4 * 32) << 16;
   const int sw = lr & 7;                   // 128-byte swizzle phase of this row
   const int m = a.m;
-  // Outliers: with m <= 4 the 4 warps sharing a row split its entries (every 4th) and each
+  // Outliers: with m <= 4 the 4 warps sharing a row split its entries (every 4th, starting at
+  // (par + lane) % 4 so that rows with fewer than 4 entries spread evenly over the warps) and each
   // accumulates tokens 0..3; with more tokens each warp takes all entries for its own 4 tokens.
   const bool split = m <= 4;
   const int otok = split ? 0 : par * 4;          // first token of oacc
-  const int ofirst = split ? par : 0, ostep = split ? 4 : 1;
+  const int ofirst = split ? ((par + lane) & 3) : 0, ostep = split ? 4 : 1;
   const bool do_out_warp = a.entries != nullptr && otok < m;
   int64_t i = 0, seg = 0;
   int s = 0, ai = 0;                      // stage ring slot; this warp's A slot is 4 * ai + par
@@ -308,6 +285,7 @@ __device__ void tc_dequant(const TcShared& S, const TcArgs& a, int64_t u0, int64
         const int slot = 4 * ai + par;
         // the A slot is normally free already (the ring runs 3 stages ahead of the MMA)
         if (!tc_wait(S, a, &S.aempty[slot], aph ^ 1, 5)) return;
+        __syncwarp();
         tc_fence_after();
         const uint8_t* prow = sb + tc::kPayOff + lr * 128;
         const uint4 P0 = *reinterpret_cast<const uint4*>(prow + (((2 * sub) ^ sw) << 4));
@@ -380,6 +358,7 @@ __device__ void tc_epilogue(const TcShared& S, const TcArgs& a, int64_t u0, int6
     const int d = (int)(seg & 1);
     const uint32_t ph = (uint32_t)(seg >> 1) & 1;
     if (!tc_wait(S, a, &S.dfull[d], ph, 6)) return;
+    __syncwarp();
     tc_fence_after();
     float val[16];
     tmem_ld_32x32b_x16(tmem + tc::kTmemD + d * 16 + lane_base, val);
@@ -497,52 +476,8 @@ gemv_tc_kernel(const TcArgs a, const __grid_constant__ TcMaps M) {
   }
 }
 
-static int sm_count(int dev) {
-  static int cached[64] = {0};
-  if (dev < 0 || dev >= 64) return 148;
-  if (!cached[dev]) {
-    int n = 0;
-    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
-    cached[dev] = n > 0 ? n : 148;
-  }
-  return cached[dev];
-}
-
 // ---------------------------------------------------------------------------------------
 // host: tensor maps
-typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
-                                  const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
-                                  const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
-                                  CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
-
-static EncodeTiledFn encode_fn() {
-  static EncodeTiledFn fn = nullptr;
-  if (!fn) {
-    void* p = nullptr;
-    cudaDriverEntryPointQueryResult q;
-    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
-        q == cudaDriverEntryPointSuccess)
-      fn = reinterpret_cast<EncodeTiledFn>(p);
-  }
-  return fn;
-}
-
-static int encode_2d(CUtensorMap* m, CUtensorMapDataType dt, const void* base, uint64_t inner,
-                     uint64_t rows, uint64_t row_bytes, uint32_t box_inner, uint32_t box_rows,
-                     CUtensorMapSwizzle swz) {
-  EncodeTiledFn fn = encode_fn();
-  if (!fn) return set_error(FBFP_ERR_CUDA, "cuTensorMapEncodeTiled is not available");
-  const cuuint64_t dims[2] = {inner, rows};
-  const cuuint64_t strides[1] = {row_bytes};
-  const cuuint32_t box[2] = {box_inner, box_rows};
-  const cuuint32_t es[2] = {1, 1};
-  CUresult r = fn(m, dt, 2, const_cast<void*>(base), dims, strides, box, es,
-                  CU_TENSOR_MAP_INTERLEAVE_NONE, swz, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-  if (r != CUDA_SUCCESS) return set_error(FBFP_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d)", (int)r);
-  return FBFP_OK;
-}
-
 // Activations X[m][k] (bf16, leading dim ldx) as a 2-D tensor (k, token) copied in boxes of
 // 64 k x m tokens with 128-byte swizzle: each box lands as the MMA's K-major B operand for
 // 4 blocks (token rows 8 and up in the second 1024-byte atom); columns >= k_in are zero-filled.

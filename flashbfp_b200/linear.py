@@ -46,6 +46,14 @@ def check_device_errors(device=None) -> None:
             _lib.check(L.fbfp_gemv_check(_lib.ptr(ws), _lib.ctypes.c_void_p(sptr)), "fbfp_gemv_check")
 
 
+def prefill_eligible(X: torch.Tensor, pw: PackedWeight) -> bool:
+    """Shapes the tcgen05 prefill GEMM takes; others run as 16-token GEMV launches."""
+    def a16(t):
+        return t.data_ptr() % 16 == 0
+    return (X.dtype == torch.bfloat16 and pw.kpad % 256 == 0 and pw.k_in % 8 == 0
+            and X.stride(0) % 8 == 0 and a16(X) and a16(pw.payload) and a16(pw.signs) and a16(pw.exps))
+
+
 def packed_linear(X: torch.Tensor, pw: PackedWeight, bias: torch.Tensor | None = None,
                   out_dtype: torch.dtype | None = None, with_outliers: bool = True,
                   out: torch.Tensor | None = None) -> torch.Tensor:
@@ -71,6 +79,13 @@ def packed_linear(X: torch.Tensor, pw: PackedWeight, bias: torch.Tensor | None =
     bd = _lib.dtype_code(bias.dtype, "bias") if bias is not None else 0
     ws = gemv_workspace(X.device, pw.npad)
     st = _lib.stream_ptr(X.device)
+    if M > 16 and prefill_eligible(X, pw):
+        _lib.check(L.fbfp_gemm_prefill(_lib.ptr(X), xd, M, X.stride(0), _lib.ptr(pw.exps),
+                                       _lib.ptr(pw.signs), _lib.ptr(pw.payload), pw.n_out, pw.k_in,
+                                       pw.kpad, pw.npad, _lib.ptr(entries), _lib.ptr(seg_ptr),
+                                       _lib.ptr(bias), bd, _lib.ptr(Y), yd, Y.stride(0), _lib.ptr(ws), st),
+                   "fbfp_gemm_prefill")
+        return Y
     for m0 in range(0, M, 16):
         m = min(16, M - m0)
         _lib.check(L.fbfp_gemv(_lib.ptr(X[m0:m0 + m]), xd, m, X.stride(0), _lib.ptr(pw.exps),

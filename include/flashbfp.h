@@ -109,6 +109,27 @@ int fbfp_gemv(const void* x, int x_dtype, int64_t m, int64_t ldx,
               void* y, int y_dtype, int64_t ldy,
               void* workspace, void* stream);
 
+/* ------------------------------------------------------------------------------------
+ * Fused dequant-GEMM for prefill (many tokens), tcgen05 tensor cores.
+ * Replaces oabf_gemm (triton_kernel.py:130-195, the oabf_gemm_kernel tiles of :22-86) at
+ * prefill sizes and, when `entries` is non-null, the outlier SpMV (triton_kernel.py:339-356)
+ * and bias add (:358-362) of OABFLinear.forward; same result as fbfp_gemv:
+ *   y[m, n] = sum_k x[m, k] * W_full[n, k] + bias[n], fp32 accumulate, any m >= 1.
+ * Requirements: x bf16 (16-byte aligned, ldx and k_in multiples of 8); kpad a multiple of
+ * 256; 16-byte aligned packed arrays. Outlier values enter the tensor-core product rounded to
+ * bf16 (as the reference's bf16 index_add rounds them).
+ * workspace: at least 256 bytes of zero-initialised device memory (its first word records a
+ * bounded device-side wait that gave up; fbfp_gemv_check reads and clears it); the workspace
+ * of fbfp_gemv serves. Tiles of 128 output rows x 256 tokens; no cross-CTA reduction.
+ * ---------------------------------------------------------------------------------- */
+int fbfp_gemm_prefill(const void* x, int x_dtype, int64_t m, int64_t ldx,
+                      const int8_t* exponents, const int16_t* signs, const int32_t* payload,
+                      int64_t n_out, int64_t k_in, int64_t kpad, int64_t npad,
+                      const uint32_t* entries, const int32_t* seg_ptr,
+                      const void* bias, int bias_dtype,
+                      void* y, int y_dtype, int64_t ldy,
+                      void* workspace, void* stream);
+
 /* fbfp_gemv without a caller workspace. No counterpart in the reference: it exists for
  * callers that cannot allocate device memory — a plugin inside a host application that owns
  * all GPU memory through its own pool and forbids stray cudaMalloc calls, or a thin
