@@ -36,7 +36,6 @@ import torch  # noqa: E402
 
 METRIC = "OABF dequant-GEMV HBM GB/s and decode tokens/s at 1/2/4/8 B200"
 N_LAYERS = 48
-COLUMN_PARALLEL = ("q_proj", "k_proj", "v_proj", "gate_proj", "up_proj")
 KINDS = ("qkv", "o", "gate_up", "down")
 
 
@@ -50,6 +49,8 @@ def parse():
     ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-prefill", action="store_true",
+                    help="skip the prefill GEMM and the bf16 cuBLAS decode baseline")
     return ap.parse_args()
 
 
@@ -113,8 +114,13 @@ class Clocks:
 # --------------------------------------------------------------------------------------
 # weights
 # --------------------------------------------------------------------------------------
+def _progress(rank, msg):
+    """One line to stderr per phase (multi-rank runs: shows where a stuck rank is)."""
+    print(f"[rank {rank}] {time.strftime('%H:%M:%S')} {msg}", file=sys.stderr, flush=True)
+
+
 def build_layers(n_layers, rank, world, device):
-    from flashbfp_b200 import OABFCompressor, packed, workloads
+    from flashbfp_b200 import OABFCompressor, packed, tp, workloads
     comp = OABFCompressor(16, 64)
     layers = []
     shard_bytes = {k: 0 for k in KINDS}
@@ -122,16 +128,10 @@ def build_layers(n_layers, rank, world, device):
         parts = {}
         for j, (name, (n, k)) in enumerate(workloads.GEMMA12B_LAYER.items()):
             W = workloads.decode_weight(n, k, seed=1000 + 16 * li + j, device=device)
-            thr = comp.compute_dynamic_threshold(W)             # whole-matrix statistics
-            if name in COLUMN_PARALLEL:
-                r0, r1 = rank * n // world, (rank + 1) * n // world
-                Ws = W[r0:r1]
-            else:
-                c0, c1 = rank * k // world, (rank + 1) * k // world
-                Ws = W[:, c0:c1]
-            dp, sp = comp.compress_matrix_device(Ws, threshold=thr)
+            # this rank's slice, compressed with the whole matrix's threshold
+            dp, sp = tp.compress_shard(W, name, rank, world, comp)
             parts[name] = packed.from_compressed(dp, sp, device, build_tiles=False)
-            del W, Ws, dp, sp
+            del W, dp, sp
         L = {
             "qkv": packed.concat_rows([parts["q_proj"], parts["k_proj"], parts["v_proj"]]),
             "o": parts["o_proj"].build_tiles(),
@@ -194,7 +194,9 @@ def run_ours(args):
     if world > 1:
         dist.barrier()
     m = args.m
+    _progress(rank, "building layers")
     layers, shard_bytes = build_layers(args.layers, rank, world, device)
+    _progress(rank, "layers built")
     xs, outs = step_io(layers, m, device, world)
     from flashbfp_b200 import _lib
     L = _lib.lib()
@@ -215,6 +217,9 @@ def run_ours(args):
         for kk in KINDS:                        # eager warm-up (sets kernel attributes)
             launch_kind(kk)
     torch.cuda.synchronize(device)
+    for kk in KINDS:                            # a kernel that gave up a bounded wait fails here
+        _lib.check(L.fbfp_gemv_check(_lib.ptr(ws[kk]), _lib.stream_ptr(device)), "fbfp_gemv_check")
+    _progress(rank, "eager warm-up done")
     graphs = {}
     for kk in KINDS:
         g = torch.cuda.CUDAGraph()
@@ -222,6 +227,7 @@ def run_ours(args):
             launch_kind(kk)
         graphs[kk] = g
     torch.cuda.synchronize(device)
+    _progress(rank, "graphs captured")
 
     def one_step(evs=None):
         for i, kk in enumerate(KINDS):
@@ -251,6 +257,7 @@ def run_ours(args):
         torch.cuda.synchronize(device)
         if world > 1:
             dist.barrier()
+    _progress(rank, "timed steps done")
     elapsed_ms = start.elapsed_time(stop)
     kind_ms = {kk: sum(ev[s][i].elapsed_time(ev[s][i + 1]) for s in range(K)) / K
                for i, kk in enumerate(KINDS)}
@@ -274,6 +281,11 @@ def run_ours(args):
     e2e = None
     if not args.no_e2e:
         e2e = run_e2e(args, layers, xs, stream, device, world, rank, step_bytes)
+
+    prefill = bf16 = None
+    if world == 1 and not args.no_prefill:
+        prefill = run_prefill(layers, device)
+        bf16 = run_bf16_decode(device, m=m)
 
     result = None
     if rank == 0:
@@ -315,6 +327,8 @@ def run_ours(args):
             },
             "gpu_launches": 4 * args.layers * K,
             "e2e": e2e,
+            "prefill": prefill,
+            "bf16_cublas_decode": bf16,
         }
     clocks = clk.summary()
     if rank == 0:
@@ -409,6 +423,78 @@ def run_e2e(args, layers, xs, stream, device, world, rank, step_bytes):
     return {"value": round(step_bytes / (ms * 1e-3) / 1e9, 2), "unit": "GB/s",
             "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "ms_per_step": round(ms, 5),
             "steps": K, "api": "OABFLinear.forward in a CUDA graph"}
+
+
+def run_prefill(layers, device, m=2048, iters=10):
+    """Prefill GEMM (tensor-bound): the gate|up linear of layer 0 at m bf16 tokens, through
+    packed_linear (fbfp_gemm_prefill), beside cuBLAS bf16 on a dense bf16 weight of the same
+    shape. CUDA events on the launching stream; 3 warm-up launches."""
+    from flashbfp_b200 import workloads
+    from flashbfp_b200.linear import packed_linear, check_device_errors
+    pw = layers[0]["gate_up"]
+    X = workloads.activations(m, pw.k_in, seed=11, device=device)
+    Y = torch.empty(m, pw.n_out, dtype=torch.bfloat16, device=device)
+    Wb = (torch.randn(pw.n_out, pw.k_in, device=device) * 0.02).to(torch.bfloat16)
+    flops = 2.0 * m * pw.n_out * pw.k_in
+
+    def timed(fn):
+        for _ in range(3):
+            fn()
+        torch.cuda.synchronize(device)
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        for _ in range(iters):
+            fn()
+        b.record()
+        torch.cuda.synchronize(device)
+        return a.elapsed_time(b) / iters
+
+    ms = timed(lambda: packed_linear(X, pw, out=Y))
+    check_device_errors(device)
+    ms_b = timed(lambda: torch.matmul(X, Wb.t()))
+    peaks = _peaks()
+    tf = flops / (ms * 1e-3) / 1e12
+    return {"workload": f"prefill: gate|up {pw.n_out}x{pw.k_in} OABF at M={m} bf16 tokens",
+            "m": m, "ms": round(ms, 4), "tflops": round(tf, 1),
+            "roofline": {"bound": "tensor", "achieved": round(tf, 1), "peak": peaks["bf16_tflops"],
+                         "unit": "TFLOP/s", "frac": round(tf / peaks["bf16_tflops"], 4),
+                         "peak_source": peaks["source"], "kernel": "prefill_tc_kernel"},
+            "cublas_bf16_tflops": round(flops / (ms_b * 1e-3) / 1e12, 1),
+            "cublas_bf16_note": "torch.matmul on a dense bf16 weight of the same shape (uncompressed)"}
+
+
+def run_bf16_decode(device, m=1, n_layers=8, iters=50):
+    """The same decode step with uncompressed bf16 weights through cuBLAS (F.linear), timed on
+    n_layers layers (inputs larger than L2) and scaled to 48 layers; the bf16 baseline that the
+    compressed format is meant to beat."""
+    from flashbfp_b200 import workloads
+    shapes = {"qkv": (8192, 3840), "o": (3840, 4096), "gate_up": (30720, 3840), "down": (3840, 15360)}
+    Ws = [{kk: (torch.randn(n, k, device=device) * 0.02).to(torch.bfloat16) for kk, (n, k) in shapes.items()}
+          for _ in range(n_layers)]
+    xs = {kk: workloads.activations(m, k, seed=3, device=device) for kk, (n, k) in shapes.items()}
+
+    def step():
+        for Ly in Ws:
+            for kk in shapes:
+                torch.nn.functional.linear(xs[kk], Ly[kk])
+
+    for _ in range(3):
+        step()
+    torch.cuda.synchronize(device)
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    for _ in range(iters):
+        step()
+    b.record()
+    torch.cuda.synchronize(device)
+    ms48 = a.elapsed_time(b) / iters * N_LAYERS / n_layers
+    byts = sum(2 * n * k for n, k in shapes.values()) * N_LAYERS
+    del Ws
+    torch.cuda.empty_cache()
+    return {"layers_timed": n_layers, "ms_per_step_48_layers": round(ms48, 4),
+            "decode_tokens_per_s": round(m * 1000.0 / ms48, 1),
+            "weight_gbs": round(byts / (ms48 * 1e-3) / 1e9, 1),
+            "note": "uncompressed bf16 weights, torch F.linear (cuBLAS), eager launches"}
 
 
 def _peaks():

@@ -1,5 +1,5 @@
 // sm100.cuh — thin wrappers over the sm_100a PTX used by the warp-specialised kernels:
-// mbarriers (with bounded waits), bulk async copies (TMA, no multicast), and tcgen05
+// mbarriers (with bounded waits), bulk async copies (TMA into this CTA only), and tcgen05
 // tensor-memory allocation, loads/stores, MMA and commit.
 #pragma once
 #include <stdint.h>
@@ -56,7 +56,7 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, uint32
 
 // ---------------------------------------------------------------- bulk copies
 // 1-D bulk copy global -> shared completing on an mbarrier (size and both addresses
-// must be multiples of 16 bytes). No multicast.
+// must be multiples of 16 bytes); the destination is this CTA's shared memory.
 __device__ __forceinline__ void bulk_g2s(void* dst_smem, const void* src_gmem, uint32_t bytes,
                                          uint64_t* bar) {
   asm volatile(
@@ -64,7 +64,7 @@ __device__ __forceinline__ void bulk_g2s(void* dst_smem, const void* src_gmem, u
       ::"r"(smem_u32(dst_smem)), "l"(src_gmem), "r"(bytes), "r"(smem_u32(bar)) : "memory");
 }
 // Tiled tensor copies (TMA) global -> shared completing on an mbarrier. The tensor map
-// lives in kernel-parameter space (__grid_constant__). No multicast.
+// lives in kernel-parameter space (__grid_constant__); the destination is this CTA's shared memory.
 __device__ __forceinline__ void tma_2d_g2s(void* dst_smem, const void* tmap, int x, int y, uint64_t* bar) {
   asm volatile(
       "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];\n"

@@ -119,8 +119,9 @@ def concat_rows(parts: List[PackedWeight]) -> PackedWeight:
     return pw.build_tiles()
 
 
-def shard_rows(pw: PackedWeight, r0: int, r1: int) -> PackedWeight:
-    """Output rows [r0, r1) (column-parallel shard); r0, r1 multiples of 16."""
+def shard_rows(pw: PackedWeight, r0: int, r1: int, tiles: bool = True) -> PackedWeight:
+    """Output rows [r0, r1) (column-parallel shard); r0, r1 multiples of 16. ``tiles=False``
+    keeps only the COO outliers (no kernel layout; works on CPU tensors)."""
     assert r0 % 16 == 0 and (r1 % 16 == 0 or r1 == pw.npad) and 0 <= r0 < r1 <= pw.npad
     kb = pw.kb_row
     exps = pw.exps[r0 * kb:r1 * kb].contiguous()
@@ -133,11 +134,12 @@ def shard_rows(pw: PackedWeight, r0: int, r1: int) -> PackedWeight:
         coo = ((b[keep] - r0 * kb).contiguous(), o[keep].contiguous(), v[keep].contiguous())
     n_out = max(0, min(pw.n_out, r1) - r0)
     out = PackedWeight(exps, signs, payload, n_out, pw.k_in, pw.kpad, r1 - r0, coo)
-    return out.build_tiles()
+    return out.build_tiles() if tiles else out
 
 
-def shard_cols(pw: PackedWeight, kb0: int, kb1: int) -> PackedWeight:
-    """Input block-columns [kb0, kb1) (row-parallel shard): K range [16*kb0, 16*kb1)."""
+def shard_cols(pw: PackedWeight, kb0: int, kb1: int, tiles: bool = True) -> PackedWeight:
+    """Input block-columns [kb0, kb1) (row-parallel shard): K range [16*kb0, 16*kb1).
+    ``tiles=False`` keeps only the COO outliers (works on CPU tensors)."""
     kb = pw.kb_row
     assert 0 <= kb0 < kb1 <= kb
     nkb = kb1 - kb0
@@ -153,4 +155,4 @@ def shard_cols(pw: PackedWeight, kb0: int, kb1: int) -> PackedWeight:
                v[keep].contiguous())
     k_in = max(0, min(pw.k_in, 16 * kb1) - 16 * kb0)
     out = PackedWeight(exps, signs, payload, pw.n_out, k_in, 16 * nkb, pw.npad, coo)
-    return out.build_tiles()
+    return out.build_tiles() if tiles else out

@@ -1,0 +1,109 @@
+"""Tensor parallelism for OABF linears: one process per GPU, torch.distributed for the exchange.
+
+Column-parallel linears (q/k/v/gate/up: they share the layer input and feed per-head or
+element-wise work) keep a slice of output rows on every rank and need no collective.
+Row-parallel linears (o/down: their input is already sharded by the previous column-parallel
+layer) keep a slice of input block-columns and add their fp32 partial outputs with one
+all-reduce. The outlier threshold of the reference is a whole-matrix statistic
+(flash_bfp/compressor.py:11-32), so every shard is compressed with the threshold of the whole
+matrix; its bytes then equal the corresponding slice of the whole matrix's compression.
+"""
+from __future__ import annotations
+
+from typing import Optional, Tuple
+
+import torch
+
+from . import packed
+
+COLUMN_PARALLEL = ("q_proj", "k_proj", "v_proj", "gate_proj", "up_proj")
+ROW_PARALLEL = ("o_proj", "down_proj")
+
+
+def mode_of(name: str) -> str:
+    """'column' or 'row' for a linear's module name (matched by suffix)."""
+    base = name.rsplit(".", 1)[-1]
+    if base in COLUMN_PARALLEL:
+        return "column"
+    if base in ROW_PARALLEL:
+        return "row"
+    raise ValueError(f"no tensor-parallel mode for {name!r}")
+
+
+def split(total: int, rank: int, world: int, align: int = 1) -> Tuple[int, int]:
+    """[lo, hi) of an even split of `total` items in units of `align` (remainder to the last)."""
+    if not 0 <= rank < world:
+        raise ValueError(f"rank {rank} outside world {world}")
+    units = (total + align - 1) // align
+    lo = rank * units // world * align
+    hi = min(total, (rank + 1) * units // world * align)
+    return lo, hi
+
+
+def weight_slice(W: torch.Tensor, name: str, rank: int, world: int) -> torch.Tensor:
+    """This rank's part of W [N, K]: output rows (column-parallel) or a K range in whole
+    16-column blocks (row-parallel)."""
+    n, k = W.shape
+    if mode_of(name) == "column":
+        r0, r1 = split(n, rank, world, align=16)
+        return W[r0:r1]
+    c0, c1 = split(k, rank, world, align=16)
+    return W[:, c0:c1]
+
+
+def input_range(name: str, k: int, rank: int, world: int) -> Tuple[int, int]:
+    """Columns of the layer input a row-parallel shard reads ([0, k) for column-parallel)."""
+    if mode_of(name) == "column":
+        return 0, k
+    return split(k, rank, world, align=16)
+
+
+def compress_shard(W: torch.Tensor, name: str, rank: int, world: int, compressor):
+    """(dense_payload, sparse_outliers) of this rank's slice, with the whole matrix's threshold."""
+    thr = compressor.compute_dynamic_threshold(W)
+    return compressor.compress_matrix_device(weight_slice(W, name, rank, world), threshold=thr)
+
+
+def slice_packed(pw: packed.PackedWeight, name: str, rank: int, world: int,
+                 tiles: bool = True) -> packed.PackedWeight:
+    """This rank's slice of a whole-matrix compression (the same bytes compress_shard makes)."""
+    if mode_of(name) == "column":
+        r0, r1 = split(pw.n_out, rank, world, align=16)
+        return packed.shard_rows(pw, r0, r1 if r1 < pw.n_out else pw.npad, tiles=tiles)
+    c0, c1 = split(pw.k_in, rank, world, align=16)
+    return packed.shard_cols(pw, c0 // 16, (c1 + 15) // 16, tiles=tiles)
+
+
+def all_reduce_sum(y: torch.Tensor, group=None) -> torch.Tensor:
+    """Sum of the ranks' fp32 partial outputs (row-parallel exchange), in place."""
+    import torch.distributed as dist
+    if dist.is_available() and dist.is_initialized() and dist.get_world_size(group) > 1:
+        dist.all_reduce(y, op=dist.ReduceOp.SUM, group=group)
+    return y
+
+
+class TPLinear(torch.nn.Module):
+    """One rank's shard of an OABF linear. forward(X) takes the full layer input for
+    column-parallel shards and returns this rank's output columns; for row-parallel shards it
+    takes the full input, reads its own K range, and returns the complete (all-reduced) output."""
+
+    def __init__(self, pw: packed.PackedWeight, name: str, rank: int, world: int, k_full: int,
+                 bias: Optional[torch.Tensor] = None, group=None):
+        super().__init__()
+        self.pw, self.mode, self.rank, self.world, self.group = pw, mode_of(name), rank, world, group
+        self.k0, self.k1 = input_range(name, k_full, rank, world)
+        self.bias = bias
+
+    def forward(self, X: torch.Tensor) -> torch.Tensor:
+        from .linear import packed_linear
+        lead = X.shape[:-1]
+        X2 = X.reshape(-1, X.shape[-1])
+        if self.mode == "column":
+            Y = packed_linear(X2, self.pw, self.bias)
+        else:
+            Y = packed_linear(X2[:, self.k0:self.k1], self.pw, None, torch.float32)
+            all_reduce_sum(Y, self.group)
+            if self.bias is not None:
+                Y = Y + self.bias.float()
+            Y = Y.to(X.dtype)
+        return Y.reshape(*lead, Y.shape[-1])
