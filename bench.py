@@ -274,6 +274,7 @@ def run_ours(args):
     if world > 1:
         dist.all_reduce(b)
     kind_bytes = {kk: float(b[i]) for i, kk in enumerate(KINDS)}
+    _progress(rank, "step timings reduced")
     step_bytes = sum(kind_bytes.values())
     value = step_bytes / (ms_per_step * 1e-3) / 1e9
 
@@ -335,14 +336,20 @@ def run_ours(args):
         result["clocks"] = clocks
         if not args.no_cpu_baseline and world == 1:
             result["cpu_baseline"] = cpu_baseline_sample(10.0)
-    # release graphs before the process group
+        print(json.dumps(result), flush=True)
+    # CUDA graphs that captured NCCL collectives go before the process group does
+    for g in graphs.values():
+        g.reset()
     del graphs
     torch.cuda.synchronize(device)
     if world > 1:
-        dist.barrier()
-        dist.destroy_process_group()
-    if rank == 0:
-        print(json.dumps(result), flush=True)
+        # Every collective of this run has completed (the step timings were all-reduced above).
+        # Tearing NCCL down after graph-captured collectives can block indefinitely, so the
+        # ranks leave without it.
+        _progress(rank, "done")
+        sys.stdout.flush()
+        sys.stderr.flush()
+        os._exit(0)
 
 
 def _gemv(L, _lib, X, pw, Y, ws):
@@ -419,6 +426,7 @@ def run_e2e(args, layers, xs, stream, device, world, rank, step_bytes):
     if world > 1:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
     ms = float(t[0])
+    g.reset()
     del g
     return {"value": round(step_bytes / (ms * 1e-3) / 1e9, 2), "unit": "GB/s",
             "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "ms_per_step": round(ms, 5),
