@@ -283,10 +283,11 @@ def run_ours(args):
     if not args.no_e2e:
         e2e = run_e2e(args, layers, xs, stream, device, world, rank, step_bytes)
 
-    prefill = bf16 = None
+    prefill = bf16 = compress = None
     if world == 1 and not args.no_prefill:
         prefill = run_prefill(layers, device)
         bf16 = run_bf16_decode(device, m=m)
+        compress = run_compress(device)
 
     result = None
     if rank == 0:
@@ -330,6 +331,7 @@ def run_ours(args):
             "e2e": e2e,
             "prefill": prefill,
             "bf16_cublas_decode": bf16,
+            "compress": compress,
         }
     clocks = clk.summary()
     if rank == 0:
@@ -469,6 +471,31 @@ def run_prefill(layers, device, m=2048, iters=10):
                          "peak_source": peaks["source"], "kernel": "prefill_tc_kernel"},
             "cublas_bf16_tflops": round(flops / (ms_b * 1e-3) / 1e12, 1),
             "cublas_bf16_note": "torch.matmul on a dense bf16 weight of the same shape (uncompressed)"}
+
+
+def run_compress(device, iters=5):
+    """GPU compressor (threshold, pack, outlier list) on a gate|up-sized bf16 matrix; HBM-bound,
+    reported as input bytes/s and as algorithmic bytes/s (input + 11 B/block + 10 B/outlier)."""
+    from flashbfp_b200 import OABFCompressor, workloads
+    n, k = 30720, 3840
+    W = workloads.decode_weight(n, k, seed=21, device=device)
+    comp = OABFCompressor()
+    for _ in range(2):
+        dp, sp = comp.compress_matrix_device(W)
+    torch.cuda.synchronize(device)
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    for _ in range(iters):
+        dp, sp = comp.compress_matrix_device(W)
+    b.record()
+    torch.cuda.synchronize(device)
+    ms = a.elapsed_time(b) / iters
+    nb = dp["exponents"].numel()
+    inp = 2.0 * n * k
+    alg = inp + 11.0 * nb + 10.0 * int(sp["count"])
+    return {"workload": f"compress_matrix_device on a {n}x{k} bf16 weight (1.5% StudentT(3) outliers)",
+            "ms": round(ms, 4), "input_gbs": round(inp / (ms * 1e-3) / 1e9, 1),
+            "algorithmic_gbs": round(alg / (ms * 1e-3) / 1e9, 1), "outliers": int(sp["count"])}
 
 
 def run_bf16_decode(device, m=1, n_layers=8, iters=50):
