@@ -115,8 +115,9 @@ class Clocks:
 # weights
 # --------------------------------------------------------------------------------------
 def _progress(rank, msg):
-    """One line to stderr per phase (multi-rank runs: shows where a stuck rank is)."""
-    print(f"[rank {rank}] {time.strftime('%H:%M:%S')} {msg}", file=sys.stderr, flush=True)
+    """One line to stderr per phase in multi-rank runs (shows where a stuck rank is)."""
+    if int(os.environ.get("WORLD_SIZE", "1")) > 1:
+        print(f"[rank {rank}] {time.strftime('%H:%M:%S')} {msg}", file=sys.stderr, flush=True)
 
 
 def build_layers(n_layers, rank, world, device):
