@@ -146,31 +146,49 @@ __device__ __forceinline__ OutRange out_range(const TcShared& S, const TcArgs& a
 }
 
 // ---------------------------------------------------------------------------------------
-// producer: four tensor copies per stage (payload, signs, exponents, activations)
+// producer: tensor copies per stage (payload, signs, exponents, activations) plus the stage's
+// outlier entries and row starts
+__device__ __forceinline__ void tc_issue_weights(const TcShared& S, const TcArgs& a, const TcMaps& M,
+                                                 int64_t u0, int64_t i, int64_t u, int s, uint32_t xbytes) {
+  uint8_t* sb = S.stage + (size_t)s * tc::kStageBytes;
+  const OutRange orr = out_range(S, a, u0, i);
+  const int rg = (int)(u / a.n_stages), st = (int)(u % a.n_stages);
+  mbar_arrive_expect_tx(&S.full[s], tc::kWeightTx + xbytes + (uint32_t)orr.n * 4 +
+                                        (a.entries ? tc::kRoffBytes : 0));
+  tma_2d_g2s(sb + tc::kPayOff, &M.pay, st * 128, rg * 128, &S.full[s]);
+  tma_2d_g2s(sb + tc::kSgnOff, &M.sgn, st * kStageKb, rg * 128, &S.full[s]);
+  tma_2d_g2s(sb + tc::kExpOff, &M.exp, st * kStageKb, rg * 128, &S.full[s]);
+  if (orr.n) bulk_g2s(sb + tc::kOutOff, a.entries + orr.lo4, (uint32_t)orr.n * 4, &S.full[s]);
+  if (a.entries) bulk_g2s(sb + tc::kRoffOff, roff_block(a, u), tc::kRoffBytes, &S.full[s]);
+}
+__device__ __forceinline__ void tc_issue_x(const TcShared& S, const TcArgs& a, const TcMaps& M,
+                                           int64_t u, int s) {
+  uint8_t* sb = S.stage + (size_t)s * tc::kStageBytes;
+  const int st = (int)(u % a.n_stages);
+#pragma unroll
+  for (int b = 0; b < 4; ++b)
+    tma_2d_g2s(sb + tc::kXOff + b * tc::kXBox, &M.x, st * 256 + b * 64, 0, &S.full[s]);
+}
+
 __device__ void tc_producer(const TcShared& S, const TcArgs& a, const TcMaps& M, int64_t u0, int64_t u1) {
   int64_t i = 0;
   if (elect_one_sync()) {
     prefetch_tmap(&M.pay); prefetch_tmap(&M.sgn); prefetch_tmap(&M.exp); prefetch_tmap(&M.x);
-    int s = 0;
-    uint32_t ph = 0;
-    int rg = (int)(u0 / a.n_stages), st = (int)(u0 % a.n_stages);
     const uint32_t xbytes = 4u * 128u * (uint32_t)a.m;          // 4 boxes of 64 k x m tokens
-    for (int64_t u = u0; u < u1; ++u, ++i) {
+    // The weights, outlier entries and row starts of the first stages do not depend on the
+    // previous kernel in the stream: fetch them before waiting for it, then the activations.
+    const int64_t npre = (u1 - u0) < tc::kStages ? (u1 - u0) : tc::kStages;
+    for (int64_t j = 0; j < npre; ++j) tc_issue_weights(S, a, M, u0, j, u0 + j, (int)j, xbytes);
+    grid_dependency_wait();
+    for (int64_t j = 0; j < npre; ++j) tc_issue_x(S, a, M, u0 + j, (int)j);
+    i = npre;
+    int s = (int)(npre % tc::kStages);
+    uint32_t ph = npre == tc::kStages ? 1u : 0u;
+    for (int64_t u = u0 + npre; u < u1; ++u, ++i) {
       if (!tc_wait(S, a, &S.empty[s], ph ^ 1, 1)) break;
-      uint8_t* sb = S.stage + (size_t)s * tc::kStageBytes;
-      const OutRange orr = out_range(S, a, u0, i);
-      mbar_arrive_expect_tx(&S.full[s], tc::kWeightTx + xbytes + (uint32_t)orr.n * 4 +
-                                            (a.entries ? tc::kRoffBytes : 0));
-      tma_2d_g2s(sb + tc::kPayOff, &M.pay, st * 128, rg * 128, &S.full[s]);
-      tma_2d_g2s(sb + tc::kSgnOff, &M.sgn, st * kStageKb, rg * 128, &S.full[s]);
-      tma_2d_g2s(sb + tc::kExpOff, &M.exp, st * kStageKb, rg * 128, &S.full[s]);
-#pragma unroll
-      for (int b = 0; b < 4; ++b)
-        tma_2d_g2s(sb + tc::kXOff + b * tc::kXBox, &M.x, st * 256 + b * 64, 0, &S.full[s]);
-      if (orr.n) bulk_g2s(sb + tc::kOutOff, a.entries + orr.lo4, (uint32_t)orr.n * 4, &S.full[s]);
-      if (a.entries) bulk_g2s(sb + tc::kRoffOff, roff_block(a, u), tc::kRoffBytes, &S.full[s]);
+      tc_issue_weights(S, a, M, u0, i, u, s, xbytes);
+      tc_issue_x(S, a, M, u, s);
       if (++s == tc::kStages) { s = 0; ph ^= 1; }
-      if (++st == a.n_stages) { st = 0; ++rg; }
     }
     // wind down: every stage issued so far must have landed before the CTA may exit
     for (int64_t j = i > tc::kStages ? i - tc::kStages : 0; j < i; ++j)
@@ -348,6 +366,7 @@ __device__ void tc_epilogue(const TcShared& S, const TcArgs& a, int64_t u0, int6
   const int m = a.m;
   const bool split = m <= 4;
   const float inv15 = 1.0f / 15.0f;
+  grid_dependency_wait();                 // the workspace and y may still be in use before this
   int64_t seg = 0;
   for (int64_t u = u0; u < u1; ++seg) {
     const int64_t rg = u / a.n_stages;
@@ -455,6 +474,9 @@ gemv_tc_kernel(const TcArgs a, const __grid_constant__ TcMaps M) {
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *S.tmem_slot;
+  // every CTA of the grid is resident (one per SM): the next kernel in the stream may launch;
+  // its CTAs start as these exit (the shared-memory footprint keeps them from sharing an SM)
+  if (threadIdx.x == 0) grid_launch_dependents();
 
   if (warp == 0) {
     tc_producer(S, a, M, u0, u1);
@@ -517,7 +539,20 @@ int launch_gemv_tc(const TcArgs& a, cudaStream_t st) {
   if ((rc = encode_x(&M.x, a.x, a.m, a.k_in, a.ldx)) != FBFP_OK) return rc;
   const int64_t nsm = sm_count(dev);
   const int64_t grid = nsm < a.total_units ? nsm : a.total_units;
-  gemv_tc_kernel<<<(unsigned)grid, tc::kThreads, tc::kSmemBytes, st>>>(a, M);
+  // programmatic stream serialisation: the launch may overlap the tail of the previous kernel
+  // in the stream; the kernel waits for it (griddepcontrol.wait) before reading activations or
+  // touching the workspace and y
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)grid);
+  cfg.blockDim = dim3(tc::kThreads);
+  cfg.dynamicSmemBytes = tc::kSmemBytes;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  FBFP_CUDA_TRY(cudaLaunchKernelEx(&cfg, gemv_tc_kernel, a, M));
   FBFP_LAUNCH_CHECK("gemv_tc_kernel");
   return FBFP_OK;
 }

@@ -224,6 +224,17 @@ __device__ __forceinline__ bool elect_one_sync() {
   return pred != 0;
 }
 
+// Programmatic dependent launch. A kernel launched with programmatic stream serialisation may
+// start while the previous kernel in the stream is still running; grid_dependency_wait() blocks
+// until that kernel has completed and its memory is visible (a no-op for ordinary launches), and
+// grid_launch_dependents() lets the next such kernel start early.
+__device__ __forceinline__ void grid_dependency_wait() {
+  asm volatile("griddepcontrol.wait;\n" ::: "memory");
+}
+__device__ __forceinline__ void grid_launch_dependents() {
+  asm volatile("griddepcontrol.launch_dependents;\n" ::: "memory");
+}
+
 // Per-warpgroup register budget change; every thread of the 4 warps of a warpgroup executes it.
 // The counts of all warpgroups must add up to no more than the block's launch registers.
 template <uint32_t R>
