@@ -376,7 +376,8 @@ def run_ours(args):
 
 
 def _gemv(L, _lib, X, pw, Y, ws):
-    _lib.check(L.fbfp_gemv(_lib.ptr(X), _lib.DTYPE_CODE[X.dtype], X.shape[0], X.stride(0),
+    gemv = L.fbfp_gemv_resident if pw.resident else L.fbfp_gemv
+    _lib.check(gemv(_lib.ptr(X), _lib.DTYPE_CODE[X.dtype], X.shape[0], X.stride(0),
                            _lib.ptr(pw.exps), _lib.ptr(pw.signs), _lib.ptr(pw.payload), pw.n_out,
                            pw.k_in, pw.kpad, pw.npad, _lib.ptr(pw.entries if pw.nnz else None),
                            _lib.ptr(pw.seg_ptr if pw.nnz else None), None, 0, _lib.ptr(Y),

@@ -39,6 +39,9 @@ _PROTOS = {
                            _c_i64, _vp, _vp, _vp, _c_int, _vp, _c_int, _c_i64, _vp, _vp]),
     "fbfp_gemv_noalloc": (_c_int, [_vp, _c_int, _c_i64, _c_i64, _vp, _vp, _vp, _c_i64, _c_i64, _c_i64,
                                    _c_i64, _vp, _vp, _vp, _c_int, _vp, _c_int, _c_i64, _vp]),
+    "fbfp_gemv_resident": (_c_int, [_vp, _c_int, _c_i64, _c_i64, _vp, _vp, _vp, _c_i64, _c_i64, _c_i64,
+                                    _c_i64, _vp, _vp, _vp, _c_int, _vp, _c_int, _c_i64, _vp, _vp]),
+    "fbfp_stream_fence": (_c_int, [_vp]),
     "fbfp_gemm_prefill": (_c_int, [_vp, _c_int, _c_i64, _c_i64, _vp, _vp, _vp, _c_i64, _c_i64, _c_i64,
                                    _c_i64, _vp, _vp, _vp, _c_int, _vp, _c_int, _c_i64, _vp, _vp]),
     "fbfp_compress_scratch_bytes": (_c_i64, [_c_i64, _c_i64, _c_i64, _c_i64]),

@@ -349,12 +349,14 @@ extern "C" int fbfp_gemv_check(void* workspace, void* stream) {
   return FBFP_OK;
 }
 
-extern "C" int fbfp_gemv(const void* x, int x_dtype, int64_t m, int64_t ldx,
-                         const int8_t* exponents, const int16_t* signs, const int32_t* payload,
-                         int64_t n_out, int64_t k_in, int64_t kpad, int64_t npad,
-                         const uint32_t* entries, const int32_t* seg_ptr, const void* bias,
-                         int bias_dtype, void* y, int y_dtype, int64_t ldy, void* workspace,
-                         void* stream) {
+// resident != 0: the packed weights and outlier index were not written by the previous kernel in
+// the stream, so the tcgen05 kernel may fetch its first weight stages before that kernel ends.
+static int gemv_impl(const void* x, int x_dtype, int64_t m, int64_t ldx,
+                     const int8_t* exponents, const int16_t* signs, const int32_t* payload,
+                     int64_t n_out, int64_t k_in, int64_t kpad, int64_t npad,
+                     const uint32_t* entries, const int32_t* seg_ptr, const void* bias,
+                     int bias_dtype, void* y, int y_dtype, int64_t ldy, void* workspace,
+                     void* stream, int resident) {
   FBFP_CHECK_ARG(x && exponents && signs && payload && y && workspace, "null pointer");
   FBFP_CHECK_ARG(m >= 1 && m <= 16, "fbfp_gemv needs 1 <= m <= 16 (got %lld)", (long long)m);
   FBFP_CHECK_ARG(dtype_ok(x_dtype), "x_dtype must be f32, bf16 or f16");
@@ -394,6 +396,7 @@ extern "C" int fbfp_gemv(const void* x, int x_dtype, int64_t m, int64_t ldx,
     t.ws = a.ws; t.counters = a.counters; t.err = errp;
     t.n_stages = (int)(kb_row / kStageKb);
     t.total_units = ((npad + kGroupRows - 1) / kGroupRows) * t.n_stages;
+    t.early_weights = resident ? 1 : 0;
     return launch_gemv_tc(t, st);
   }
   const dim3 grid((unsigned)((npad + kRowsPerCta - 1) / kRowsPerCta), (unsigned)n_chunks);
@@ -408,5 +411,35 @@ extern "C" int fbfp_gemv(const void* x, int x_dtype, int64_t m, int64_t ldx,
     gemv_kernel<2><<<grid, kGemvThreads, smem, st>>>(a);
   }
   FBFP_LAUNCH_CHECK("gemv_kernel");
+  return FBFP_OK;
+}
+
+extern "C" int fbfp_gemv(const void* x, int x_dtype, int64_t m, int64_t ldx,
+                         const int8_t* exponents, const int16_t* signs, const int32_t* payload,
+                         int64_t n_out, int64_t k_in, int64_t kpad, int64_t npad,
+                         const uint32_t* entries, const int32_t* seg_ptr, const void* bias,
+                         int bias_dtype, void* y, int y_dtype, int64_t ldy, void* workspace,
+                         void* stream) {
+  return gemv_impl(x, x_dtype, m, ldx, exponents, signs, payload, n_out, k_in, kpad, npad, entries,
+                   seg_ptr, bias, bias_dtype, y, y_dtype, ldy, workspace, stream, 0);
+}
+
+extern "C" int fbfp_gemv_resident(const void* x, int x_dtype, int64_t m, int64_t ldx,
+                                  const int8_t* exponents, const int16_t* signs, const int32_t* payload,
+                                  int64_t n_out, int64_t k_in, int64_t kpad, int64_t npad,
+                                  const uint32_t* entries, const int32_t* seg_ptr, const void* bias,
+                                  int bias_dtype, void* y, int y_dtype, int64_t ldy, void* workspace,
+                                  void* stream) {
+  return gemv_impl(x, x_dtype, m, ldx, exponents, signs, payload, n_out, k_in, kpad, npad, entries,
+                   seg_ptr, bias, bias_dtype, y, y_dtype, ldy, workspace, stream, 1);
+}
+
+namespace fbfp {
+__global__ void stream_fence_kernel() {}
+}  // namespace fbfp
+
+extern "C" int fbfp_stream_fence(void* stream) {
+  stream_fence_kernel<<<1, 32, 0, as_stream(stream)>>>();
+  FBFP_LAUNCH_CHECK("stream_fence_kernel");
   return FBFP_OK;
 }

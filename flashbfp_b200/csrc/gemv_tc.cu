@@ -54,21 +54,23 @@ constexpr int kRoffBytes = 272;
 constexpr int kStageBytes = kRoffOff + 1024;                  // 39936 (multiple of 1024)
 constexpr uint32_t kWeightTx = kXOff;                        // payload + signs + exponents bytes
 constexpr int kSegCache = 1024;                               // segment pointers cached per CTA
-constexpr int kDq = 16;
-static_assert(kASlots % 4 == 0, "each dequantiser warp owns every 4th A slot");                         // dequantiser warps (2..17), 4 per lane quarter
+constexpr int kDqPerQuarter = 3;                 // dequantiser warps per tensor-memory lane quarter
+constexpr int kDq = 4 * kDqPerQuarter;
+static_assert(kASlots == 4 * kDqPerQuarter, "dequantiser warp p of a quarter owns A slots 4p..4p+3");                         // dequantiser warps (2..17), 4 per lane quarter
 constexpr int kEpiWarp0 = 4;                    // epilogue warpgroup: warps 4-7
 constexpr int kDqWarp0 = 8;                     // dequantisers: warps 8 .. 8 + kDq - 1
-constexpr int kThreads = 32 * (kDqWarp0 + kDq); // 768: 6 warps per SM sub-partition at 80 registers
+constexpr int kOutWarp0 = kDqWarp0 + kDq;       // outlier warpgroup: warps 20-23
+constexpr int kThreads = 32 * (kOutWarp0 + 4);  // 768: 6 warps per SM sub-partition
 static_assert(kDq % 4 == 0, "dequantisers come in whole warpgroups");
 constexpr uint32_t kTmemCols = 512;
 constexpr uint32_t kTmemD = 0;                  // 2 accumulators x 16 columns
 constexpr uint32_t kTmemA = 32;                 // 12 slots x 32 columns (4 blocks x 8)
 constexpr size_t kSoutOff = (size_t)kStages * kStageBytes;
 constexpr size_t kSegOff = kSoutOff;
-// outlier partial sums handed from dequantisers to the epilogue: [2 accumulators][4 warps of a
-// row][4 tokens][128 rows] fp32
+// outlier sums handed from the outlier warps to the epilogue: [2 accumulators][16 tokens][128 rows]
+// fp32 (one lane owns each row, so plain stores)
 constexpr size_t kOaccOff = kSegOff + (kSegCache + 8) * sizeof(int32_t);
-constexpr size_t kOaccBytes = 2 * 4 * 4 * 128 * sizeof(float);
+constexpr size_t kOaccBytes = 2 * 16 * 128 * sizeof(float);
 constexpr size_t kBarOff = kOaccOff + kOaccBytes;
 constexpr int kNumBars = 2 * kStages + 2 * kASlots + 8;
 constexpr size_t kSmemBytes = kBarOff + kNumBars * 8 + 16 + 1024;   // + alignment slack
@@ -83,7 +85,7 @@ struct TcShared {
   float* s_out;
   int32_t* seg;          // seg_ptr[u0 .. u0 + kSegCache]
   uint64_t *full, *empty, *afull, *aempty, *dfull, *dempty, *ofull, *oempty;
-  float* oacc;           // [2][4][4][128]
+  float* oacc;           // [2][16][128]
   uint32_t* tmem_slot;
   volatile int* abort_flag;
 };
@@ -175,8 +177,9 @@ __device__ void tc_producer(const TcShared& S, const TcArgs& a, const TcMaps& M,
   if (elect_one_sync()) {
     prefetch_tmap(&M.pay); prefetch_tmap(&M.sgn); prefetch_tmap(&M.exp); prefetch_tmap(&M.x);
     const uint32_t xbytes = 4u * 128u * (uint32_t)a.m;          // 4 boxes of 64 k x m tokens
-    // The weights, outlier entries and row starts of the first stages do not depend on the
-    // previous kernel in the stream: fetch them before waiting for it, then the activations.
+    // With resident weights (early_weights) the first stages' weights, outlier entries and row
+    // starts are fetched before waiting for the previous kernel in the stream, then the
+    // activations (otherwise the kernel has already waited and both waits are one).
     const int64_t npre = (u1 - u0) < tc::kStages ? (u1 - u0) : tc::kStages;
     for (int64_t j = 0; j < npre; ++j) tc_issue_weights(S, a, M, u0, j, u0 + j, (int)j, xbytes);
     grid_dependency_wait();
@@ -239,117 +242,128 @@ __device__ void tc_mma(const TcShared& S, const TcArgs& a, int64_t u0, int64_t u
   }
 }
 
-// Outliers of row lr in one stage (their dense slots are +0): oacc[t] += v * x[otok + t] for
-// NT tokens over the row's entries first, first + step, ...; x comes from the stage's activation
-// tile: column c of token t is in box c / 64, 1024-byte atom t / 8, 128-byte row t % 8, 16-byte
-// chunk ((c % 64) / 8) ^ (t % 8) (128-byte swizzle), element c % 8.
+// Outliers of row lr in one stage (their dense slots are +0): oacc[t] += v * x[t] for the first
+// NT tokens over all the row's entries; x comes from the stage's activation tile: column c of
+// token t is in box c / 64, 1024-byte atom t / 8, 128-byte row t % 8, 16-byte chunk
+// ((c % 64) / 8) ^ (t % 8) (128-byte swizzle), element c % 8.
 template <int NT>
 __device__ __forceinline__ void tc_row_outliers(const uint8_t* sb, const OutRange& orr,
-                                                const uint32_t* entries, int lr, int first, int step,
-                                                int otok, float* oacc) {
+                                                const uint32_t* entries, int lr, float* oacc) {
   const uint16_t* ro = reinterpret_cast<const uint16_t*>(sb + tc::kRoffOff);
   const uint32_t* es = reinterpret_cast<const uint32_t*>(sb + tc::kOutOff);
-  const uint8_t* xs = sb + tc::kXOff + (otok >> 3) * 1024;
+  const uint8_t* xs = sb + tc::kXOff;
   const int e_end = ro[lr + 1];
   const int obase = orr.lo - orr.lo4;
-  for (int t = ro[lr] + first; t < e_end; t += step) {
-    const int o = obase + t;
-    const uint32_t e = o < orr.n ? es[o] : __ldg(entries + orr.lo + t);
+  for (int k = ro[lr]; k < e_end; ++k) {
+    const int o = obase + k;
+    const uint32_t e = o < orr.n ? es[o] : __ldg(entries + orr.lo + k);
     const float v = __half2float(__ushort_as_half((unsigned short)(e & 0xFFFFu)));
     // box * 2048 + (c % 8) * 2 from bits 22-23 and 16-18 of the entry; chunk from bits 19-21
     const uint8_t* xp = xs + (((e >> 11) & 0x1800u) | ((e >> 15) & 0xEu));
     const uint32_t chunk = (e >> 19) & 7u;
 #pragma unroll
-    for (int tt = 0; tt < NT; ++tt) {
-      const uint32_t r = (uint32_t)((otok + tt) & 7);
-      const uint32_t off = (r << 7) | ((chunk ^ r) << 4);
-      oacc[tt] = fmaf(v, __uint_as_float((uint32_t)*reinterpret_cast<const uint16_t*>(xp + off) << 16),
-                      oacc[tt]);
+    for (int t = 0; t < NT; ++t) {
+      const uint32_t r = (uint32_t)(t & 7);
+      const uint32_t off = (uint32_t)(t >> 3) * 1024u + (r << 7) + ((chunk ^ r) << 4);
+      oacc[t] = fmaf(v, __uint_as_float((uint32_t)*reinterpret_cast<const uint16_t*>(xp + off) << 16),
+                     oacc[t]);
     }
   }
 }
 
-// Dequantisers: dense blocks into the tensor-memory A ring, outliers, segment epilogue.
+// Dequantisers: warp p of a lane quarter takes the stages i = p (mod 3) of the CTA's units, all
+// 16 blocks of each for its 32 rows, so the three warps of a sub-partition work on different
+// stages. Substage c of stage i goes to A slot 4p + c (the 12-slot ring holds 3 stages).
 __device__ void tc_dequant(const TcShared& S, const TcArgs& a, int64_t u0, int64_t u1, uint32_t tmem) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int wi = warp - tc::kDqWarp0;     // 0..kDq-1
   const int q4 = warp & 3;                 // tensor-memory lane quarter
-  const int par = wi >> 2;                 // which of the 4 substages of a stage (and token quarter)
+  const int par = wi >> 2;                 // this warp's stages: i = par (mod 3)
   const int lr = q4 * 32 + lane;           // row within the group
   const uint32_t lane_base = (uint32_t)(q4 * 32) << 16;
   const int sw = lr & 7;                   // 128-byte swizzle phase of this row
+  int i = 0;                               // local unit index
+  for (int64_t u = u0; u < u1; ++u, ++i) {
+    if (i % tc::kDqPerQuarter != par) continue;
+    const int s = i % tc::kStages;
+    if (!tc_wait(S, a, &S.full[s], (uint32_t)(i / tc::kStages) & 1, 4)) return;
+    const uint8_t* sb = S.stage + (size_t)s * tc::kStageBytes;
+    const uint32_t aph = (uint32_t)(i / tc::kDqPerQuarter) & 1;
+    const uint8_t* prow = sb + tc::kPayOff + lr * 128;
+    const uint4 SGv = *reinterpret_cast<const uint4*>(sb + tc::kSgnOff + lr * 32);
+    const uint4 SGw = *reinterpret_cast<const uint4*>(sb + tc::kSgnOff + lr * 32 + 16);
+    const uint4 EXv = *reinterpret_cast<const uint4*>(sb + tc::kExpOff + lr * 16);
+    const uint32_t sgw[8] = {SGv.x, SGv.y, SGv.z, SGv.w, SGw.x, SGw.y, SGw.z, SGw.w};
+    const uint32_t exw[4] = {EXv.x, EXv.y, EXv.z, EXv.w};
+#pragma unroll
+    for (int c = 0; c < 4; ++c) {            // substages (4 blocks each)
+      const int slot = 4 * par + c;
+      const uint4 P0 = *reinterpret_cast<const uint4*>(prow + (((2 * c) ^ sw) << 4));
+      const uint4 P1 = *reinterpret_cast<const uint4*>(prow + (((2 * c + 1) ^ sw) << 4));
+      const uint32_t E = (exw[c] ^ 0x80808080u) + 0x06060606u;   // e + 134 per byte
+      const uint32_t sg0 = sgw[2 * c], sg1 = sgw[2 * c + 1];
+      if (!tc_wait(S, a, &S.aempty[slot], aph ^ 1, 5)) return;
+      __syncwarp();
+      tc_fence_after();
+      // rows past npad arrive as zero bytes (TMA fill) and dequantise to +0
+      const uint32_t ta = tmem + tc::kTmemA + slot * 32 + lane_base;
+      uint32_t w[8];
+      dq_block(P0.x, P0.y, sg0 & 0xFFFFu, E & 0xFFu, w);
+      tmem_st_32x32b_x8(ta + 0, w);
+      dq_block(P0.z, P0.w, sg0 >> 16, (E >> 8) & 0xFFu, w);
+      tmem_st_32x32b_x8(ta + 8, w);
+      dq_block(P1.x, P1.y, sg1 & 0xFFFFu, (E >> 16) & 0xFFu, w);
+      tmem_st_32x32b_x8(ta + 16, w);
+      dq_block(P1.z, P1.w, sg1 >> 16, E >> 24, w);
+      tmem_st_32x32b_x8(ta + 24, w);
+      tmem_wait_st();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&S.afull[slot]);
+    }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&S.empty[s]);
+  }
+}
+
+// Outlier warps (one per lane quarter, one row per lane): every stage, the row's outlier entries
+// times the activations in fp32 (their dense slots are +0); at each segment end the sums go to
+// the epilogue through shared memory.
+__device__ void tc_outliers(const TcShared& S, const TcArgs& a, int64_t u0, int64_t u1) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int q4 = warp & 3;
+  const int lr = q4 * 32 + lane;
   const int m = a.m;
-  // Outliers: with m <= 4 the 4 warps sharing a row split its entries (every 4th, starting at
-  // (par + lane) % 4 so that rows with fewer than 4 entries spread evenly over the warps) and each
-  // accumulates tokens 0..3; with more tokens each warp takes all entries for its own 4 tokens.
-  const bool split = m <= 4;
-  const int otok = split ? 0 : par * 4;          // first token of oacc
-  const int ofirst = split ? ((par + lane) & 3) : 0, ostep = split ? 4 : 1;
-  const bool do_out_warp = a.entries != nullptr && otok < m;
-  int64_t i = 0, seg = 0;
-  int s = 0, ai = 0;                      // stage ring slot; this warp's A slot is 4 * ai + par
-  uint32_t sph = 0, aph = 0;
+  int64_t seg = 0;
+  int i = 0;
   for (int64_t u = u0; u < u1; ++seg) {
     const int64_t rg = u / a.n_stages;
     const int64_t seg_end = min(u1, (rg + 1) * a.n_stages);
-    const int64_t row = rg * 128 + lr;
-    const bool rvalid = row < a.npad;
-    float oacc[4] = {0.f, 0.f, 0.f, 0.f};
+    const bool rvalid = rg * 128 + lr < a.npad;
+    float oacc[16];
+#pragma unroll
+    for (int t = 0; t < 16; ++t) oacc[t] = 0.f;
     for (; u < seg_end; ++u, ++i) {
-      if (!tc_wait(S, a, &S.full[s], sph, 4)) return;
+      const int s = i % tc::kStages;
+      if (!tc_wait(S, a, &S.full[s], (uint32_t)(i / tc::kStages) & 1, 10)) return;
       const uint8_t* sb = S.stage + (size_t)s * tc::kStageBytes;
-      {
-        const int sub = par;
-        const int slot = 4 * ai + par;
-        // the A slot is normally free already (the ring runs 3 stages ahead of the MMA)
-        if (!tc_wait(S, a, &S.aempty[slot], aph ^ 1, 5)) return;
-        __syncwarp();
-        tc_fence_after();
-        const uint8_t* prow = sb + tc::kPayOff + lr * 128;
-        const uint4 P0 = *reinterpret_cast<const uint4*>(prow + (((2 * sub) ^ sw) << 4));
-        const uint4 P1 = *reinterpret_cast<const uint4*>(prow + (((2 * sub + 1) ^ sw) << 4));
-        const uint2 SG = *reinterpret_cast<const uint2*>(sb + tc::kSgnOff + lr * 32 + sub * 8);
-        const uint32_t EX = *reinterpret_cast<const uint32_t*>(sb + tc::kExpOff + lr * 16 + sub * 4);
-        const uint32_t E = (EX ^ 0x80808080u) + 0x06060606u;     // e + 134 per byte
-        // rows past npad arrive as zero bytes (TMA fill) and dequantise to +0
-        const uint32_t ta = tmem + tc::kTmemA + slot * 32 + lane_base;
-        uint32_t w[8];
-        dq_block(P0.x, P0.y, SG.x & 0xFFFFu, E & 0xFFu, w);
-        tmem_st_32x32b_x8(ta + 0, w);
-        dq_block(P0.z, P0.w, SG.x >> 16, (E >> 8) & 0xFFu, w);
-        tmem_st_32x32b_x8(ta + 8, w);
-        dq_block(P1.x, P1.y, SG.y & 0xFFFFu, (E >> 16) & 0xFFu, w);
-        tmem_st_32x32b_x8(ta + 16, w);
-        dq_block(P1.z, P1.w, SG.y >> 16, E >> 24, w);
-        tmem_st_32x32b_x8(ta + 24, w);
-        tmem_wait_st();
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&S.afull[slot]);
-      }
-      if (do_out_warp) {
+      if (rvalid) {
         const OutRange orr = out_range(S, a, u0, i);
-        if (rvalid) {
-          if (m == 1) tc_row_outliers<1>(sb, orr, a.entries, lr, ofirst, ostep, otok, oacc);
-          else tc_row_outliers<4>(sb, orr, a.entries, lr, ofirst, ostep, otok, oacc);
-        }
+        if (m == 1) tc_row_outliers<1>(sb, orr, a.entries, lr, oacc);
+        else if (m <= 4) tc_row_outliers<4>(sb, orr, a.entries, lr, oacc);
+        else tc_row_outliers<16>(sb, orr, a.entries, lr, oacc);
       }
       __syncwarp();
       if (lane == 0) mbar_arrive(&S.empty[s]);
-      if (++s == tc::kStages) { s = 0; sph ^= 1; }
-      if (++ai == tc::kASlots / 4) { ai = 0; aph ^= 1; }
     }
-
-    // ---- segment end: hand the outlier partial sums to the epilogue warps ----
-    if (a.entries) {
-      const int d = (int)(seg & 1);
-      if (!tc_wait(S, a, &S.oempty[d], ((uint32_t)(seg >> 1) & 1) ^ 1, 7)) return;
-      float* so = S.oacc + (size_t)((d * 4 + par) * 4) * 128 + lr;
+    const int d = (int)(seg & 1);
+    if (!tc_wait(S, a, &S.oempty[d], ((uint32_t)(seg >> 1) & 1) ^ 1, 7)) return;
+    float* so = S.oacc + (size_t)(d * 16) * 128 + lr;
 #pragma unroll
-      for (int t = 0; t < 4; ++t) so[t * 128] = oacc[t];
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&S.ofull[d]);
-    }
+    for (int t = 0; t < 16; ++t)
+      if (t < m) so[t * 128] = oacc[t];
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&S.ofull[d]);
   }
 }
 
@@ -364,7 +378,6 @@ __device__ void tc_epilogue(const TcShared& S, const TcArgs& a, int64_t u0, int6
   const int lr = q4 * 32 + lane;
   const uint32_t lane_base = (uint32_t)(q4 * 32) << 16;
   const int m = a.m;
-  const bool split = m <= 4;
   const float inv15 = 1.0f / 15.0f;
   grid_dependency_wait();                 // the workspace and y may still be in use before this
   int64_t seg = 0;
@@ -389,15 +402,10 @@ __device__ void tc_epilogue(const TcShared& S, const TcArgs& a, int64_t u0, int6
     for (int t = 0; t < 16; ++t) val[t] *= inv15;
     if (a.entries) {
       if (!tc_wait(S, a, &S.ofull[d], ph, 8)) return;
-      const float* so = S.oacc + (size_t)(d * 16) * 128 + lr;      // [par][t][row]
-      if (split) {
+      const float* so = S.oacc + (size_t)(d * 16) * 128 + lr;     // [t][row]
 #pragma unroll
-        for (int t = 0; t < 4; ++t)
-          val[t] += (so[t * 128] + so[(4 + t) * 128]) + (so[(8 + t) * 128] + so[(12 + t) * 128]);
-      } else {
-#pragma unroll
-        for (int t = 0; t < 16; ++t) val[t] += so[t * 128];
-      }
+      for (int t = 0; t < 16; ++t)
+        if (t < m) val[t] += so[t * 128];
       __syncwarp();
       if (lane == 0) mbar_arrive(&S.oempty[d]);
     }
@@ -449,14 +457,21 @@ gemv_tc_kernel(const TcArgs a, const __grid_constant__ TcMaps M) {
   const int64_t U = a.total_units;
   const int64_t u0 = (int64_t)blockIdx.x * U / gridDim.x;
   const int64_t u1 = (int64_t)(blockIdx.x + 1) * U / gridDim.x;
+  // Programmatic launch: the previous kernel in the stream may still be running. Unless the
+  // caller vouched that it did not write the weights (fbfp_gemv_resident), read no global memory
+  // before it has completed; the barrier setup below still overlaps its tail.
+  if (!a.early_weights) grid_dependency_wait();
 
   if (threadIdx.x == 0) {
-    for (int s = 0; s < tc::kStages; ++s) { mbar_init(&S.full[s], 1); mbar_init(&S.empty[s], tc::kDq + 1); }
+    // a stage is released by the dequantiser of each lane quarter that took it, the MMA and,
+    // with outliers, the 4 outlier warps
+    const uint32_t rel = 4 + 1 + (a.entries ? 4 : 0);
+    for (int s = 0; s < tc::kStages; ++s) { mbar_init(&S.full[s], 1); mbar_init(&S.empty[s], rel); }
     for (int j = 0; j < tc::kASlots; ++j) { mbar_init(&S.afull[j], 4); mbar_init(&S.aempty[j], 1); }
     for (int d = 0; d < 2; ++d) {
       mbar_init(&S.dfull[d], 1);
       mbar_init(&S.dempty[d], 4);                 // the 4 epilogue warps
-      mbar_init(&S.ofull[d], tc::kDq);
+      mbar_init(&S.ofull[d], 4);                  // the 4 outlier warps
       mbar_init(&S.oempty[d], 4);
     }
     *S.abort_flag = 0;
@@ -485,8 +500,10 @@ gemv_tc_kernel(const TcArgs a, const __grid_constant__ TcMaps M) {
     __syncwarp();
   } else if (warp >= tc::kEpiWarp0 && warp < tc::kDqWarp0) {
     tc_epilogue(S, a, u0, u1, tmem);
-  } else if (warp >= tc::kDqWarp0) {
+  } else if (warp >= tc::kDqWarp0 && warp < tc::kOutWarp0) {
     tc_dequant(S, a, u0, u1, tmem);
+  } else if (warp >= tc::kOutWarp0 && a.entries) {
+    tc_outliers(S, a, u0, u1);
   }
 
   tc_fence_before();

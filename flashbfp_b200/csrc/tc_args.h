@@ -23,5 +23,6 @@ struct TcArgs {
   int32_t* err;
   int n_stages;          // kb_row / 16
   int64_t total_units;   // ceil(npad/128) * n_stages
+  int early_weights;     // 1: fetch the first weight stages before the grid-dependency wait
 };
 }  // namespace fbfp

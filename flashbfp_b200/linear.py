@@ -86,9 +86,10 @@ def packed_linear(X: torch.Tensor, pw: PackedWeight, bias: torch.Tensor | None =
                                        _lib.ptr(bias), bd, _lib.ptr(Y), yd, Y.stride(0), _lib.ptr(ws), st),
                    "fbfp_gemm_prefill")
         return Y
+    gemv = L.fbfp_gemv_resident if pw.resident else L.fbfp_gemv
     for m0 in range(0, M, 16):
         m = min(16, M - m0)
-        _lib.check(L.fbfp_gemv(_lib.ptr(X[m0:m0 + m]), xd, m, X.stride(0), _lib.ptr(pw.exps),
+        _lib.check(gemv(_lib.ptr(X[m0:m0 + m]), xd, m, X.stride(0), _lib.ptr(pw.exps),
                                _lib.ptr(pw.signs), _lib.ptr(pw.payload), pw.n_out, pw.k_in, pw.kpad,
                                pw.npad, _lib.ptr(entries), _lib.ptr(seg_ptr), _lib.ptr(bias), bd,
                                _lib.ptr(Y[m0:m0 + m]), yd, Y.stride(0), _lib.ptr(ws), st),

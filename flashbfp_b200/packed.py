@@ -26,6 +26,10 @@ class PackedWeight:
         self.n_out, self.k_in, self.kpad, self.npad = int(n_out), int(k_in), int(kpad), int(npad)
         self.coo = coo                  # (block_idx int32, offset int32, value bits int16)
         self.entries, self.seg_ptr = entries, seg_ptr
+        # True once a fence kernel follows the last kernel that wrote these arrays on the current
+        # stream: GEMVs may then use fbfp_gemv_resident (weight fetch overlapping the previous
+        # kernel's tail)
+        self.resident = False
 
     @property
     def device(self):
@@ -44,6 +48,7 @@ class PackedWeight:
         return 11 * self.npad * self.kb_row + 10 * self.nnz
 
     def apply(self, fn):
+        self.resident = False
         self.exps, self.signs, self.payload = fn(self.exps), fn(self.signs), fn(self.payload)
         if self.coo is not None:
             self.coo = tuple(fn(t) for t in self.coo)
@@ -68,7 +73,9 @@ class PackedWeight:
                                                   _lib.ptr(entries), _lib.ptr(seg_ptr),
                                                   _lib.ptr(scratch), _lib.stream_ptr(dev)),
                        "fbfp_outlier_tiles_build")
+            _lib.check(L.fbfp_stream_fence(_lib.stream_ptr(dev)), "fbfp_stream_fence")
         self.entries, self.seg_ptr = entries, seg_ptr
+        self.resident = True
         return self
 
 

@@ -109,6 +109,23 @@ int fbfp_gemv(const void* x, int x_dtype, int64_t m, int64_t ldx,
               void* y, int y_dtype, int64_t ldy,
               void* workspace, void* stream);
 
+/* Same as fbfp_gemv for weights already resident: the packed arrays, `entries` and `seg_ptr`
+ * must not have been written by the kernel that immediately precedes this call in `stream`
+ * (any other kernel in between, e.g. fbfp_stream_fence, suffices). The tcgen05 kernel is launched
+ * with programmatic stream serialisation and then fetches its first weight stages while the
+ * previous kernel finishes (fbfp_gemv also overlaps that kernel's tail, but reads no global
+ * memory until it has completed). No counterpart in the reference. */
+int fbfp_gemv_resident(const void* x, int x_dtype, int64_t m, int64_t ldx,
+                       const int8_t* exponents, const int16_t* signs, const int32_t* payload,
+                       int64_t n_out, int64_t k_in, int64_t kpad, int64_t npad,
+                       const uint32_t* entries, const int32_t* seg_ptr,
+                       const void* bias, int bias_dtype,
+                       void* y, int y_dtype, int64_t ldy,
+                       void* workspace, void* stream);
+/* Launches an empty kernel on `stream`: placed after the kernels that write a matrix's packed
+ * arrays, it makes the matrix resident for fbfp_gemv_resident. No counterpart in the reference. */
+int fbfp_stream_fence(void* stream);
+
 /* ------------------------------------------------------------------------------------
  * Fused dequant-GEMM for prefill (many tokens), tcgen05 tensor cores.
  * Replaces oabf_gemm (triton_kernel.py:130-195, the oabf_gemm_kernel tiles of :22-86) at
