@@ -290,18 +290,17 @@ __device__ void tc_dequant(const TcShared& S, const TcArgs& a, int64_t u0, int64
     const uint8_t* sb = S.stage + (size_t)s * tc::kStageBytes;
     const uint32_t aph = (uint32_t)(i / tc::kDqPerQuarter) & 1;
     const uint8_t* prow = sb + tc::kPayOff + lr * 128;
-    const uint4 SGv = *reinterpret_cast<const uint4*>(sb + tc::kSgnOff + lr * 32);
-    const uint4 SGw = *reinterpret_cast<const uint4*>(sb + tc::kSgnOff + lr * 32 + 16);
-    const uint4 EXv = *reinterpret_cast<const uint4*>(sb + tc::kExpOff + lr * 16);
-    const uint32_t sgw[8] = {SGv.x, SGv.y, SGv.z, SGv.w, SGw.x, SGw.y, SGw.z, SGw.w};
-    const uint32_t exw[4] = {EXv.x, EXv.y, EXv.z, EXv.w};
-#pragma unroll
+    // not unrolled: one copy of the block dequantiser keeps the kernel's code within the
+    // instruction cache next to the other roles
+#pragma unroll 1
     for (int c = 0; c < 4; ++c) {            // substages (4 blocks each)
       const int slot = 4 * par + c;
       const uint4 P0 = *reinterpret_cast<const uint4*>(prow + (((2 * c) ^ sw) << 4));
       const uint4 P1 = *reinterpret_cast<const uint4*>(prow + (((2 * c + 1) ^ sw) << 4));
-      const uint32_t E = (exw[c] ^ 0x80808080u) + 0x06060606u;   // e + 134 per byte
-      const uint32_t sg0 = sgw[2 * c], sg1 = sgw[2 * c + 1];
+      const uint2 SG = *reinterpret_cast<const uint2*>(sb + tc::kSgnOff + lr * 32 + c * 8);
+      const uint32_t EX = *reinterpret_cast<const uint32_t*>(sb + tc::kExpOff + lr * 16 + c * 4);
+      const uint32_t E = (EX ^ 0x80808080u) + 0x06060606u;       // e + 134 per byte
+      const uint32_t sg0 = SG.x, sg1 = SG.y;
       if (!tc_wait(S, a, &S.aempty[slot], aph ^ 1, 5)) return;
       __syncwarp();
       tc_fence_after();
