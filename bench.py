@@ -49,6 +49,8 @@ def parse():
     ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--nccl", action="store_true",
+                    help="row-parallel exchange through NCCL instead of the NVLink peer-memory all-reduce")
     ap.add_argument("--no-prefill", action="store_true",
                     help="skip the prefill GEMM and the bf16 cuBLAS decode baseline")
     return ap.parse_args()
@@ -203,6 +205,16 @@ def run_ours(args):
     L = _lib.lib()
     ws = {kk: torch.zeros(L.fbfp_gemv_workspace_bytes(16, layers[0][kk].npad), dtype=torch.uint8,
                           device=device) for kk in KINDS}
+    reducer = None
+    if world > 1 and not args.nccl:
+        from flashbfp_b200.tp import NVLinkAllReduce
+        reducer = NVLinkAllReduce(16 * max(layers[0][kk].n_out for kk in ("o", "down")))
+
+    def exchange(y):
+        if reducer is not None:
+            reducer(y)
+        else:
+            dist.all_reduce(y)
 
     def launch_kind(kk):
         for li, Ly in enumerate(layers):
@@ -210,7 +222,7 @@ def run_ours(args):
             y = outs[li][kk]
             _gemv(L, _lib, xs[kk], pw, y, ws[kk])
             if kk in ("o", "down") and world > 1:
-                dist.all_reduce(y)
+                exchange(y)
 
     stream = torch.cuda.Stream(device)
     stream.wait_stream(torch.cuda.current_stream(device))
@@ -230,7 +242,7 @@ def run_ours(args):
                 y = outs[li][kk]
                 _gemv(L, _lib, xs[kk], Ly[kk], y, ws[kk])
                 if kk in ("o", "down") and world > 1:
-                    dist.all_reduce(y)
+                    exchange(y)
 
     graphs = {}
     for kk in KINDS:                            # per kind: rates and the roofline kernel
@@ -301,7 +313,7 @@ def run_ours(args):
     # ---------------- e2e through the public module API ----------------
     e2e = None
     if not args.no_e2e:
-        e2e = run_e2e(args, layers, xs, stream, device, world, rank, step_bytes)
+        e2e = run_e2e(args, layers, xs, stream, device, world, rank, step_bytes, exchange)
 
     prefill = bf16 = compress = None
     if world == 1 and not args.no_prefill:
@@ -334,6 +346,9 @@ def run_ours(args):
                              "12B-class layers (q|k|v 8192x3840, o 3840x4096, gate|up 30720x3840, "
                              "down 3840x15360; OABF block 16, 1.5% StudentT(3)x20 outliers)"),
                 "m": m, "layers": args.layers, "parallelism": f"tp{world}",
+                "exchange": (None if world == 1 else
+                             "NCCL all-reduce" if args.nccl else
+                             "one-shot all-reduce over NVLink peer memory (csrc/allreduce.cu)"),
                 "launches_per_step": 4 * args.layers,
                 "l2": "inputs larger than L2 (%.2f GB packed per step per rank)" % (step_bytes / world / 1e9),
                 "graphs": ("one CUDA graph per step (192 launches in model order, programmatic "
@@ -385,7 +400,7 @@ def _gemv(L, _lib, X, pw, Y, ws):
                            _lib.stream_ptr(X.device)), "fbfp_gemv")
 
 
-def run_e2e(args, layers, xs, stream, device, world, rank, step_bytes):
+def run_e2e(args, layers, xs, stream, device, world, rank, step_bytes, exchange):
     """Public-API step: OABFLinear modules in a CUDA graph; host activations in, outputs out."""
     import torch.distributed as dist
     from flashbfp_b200.linear import OABFLinear
@@ -409,7 +424,7 @@ def run_e2e(args, layers, xs, stream, device, world, rank, step_bytes):
                 y = mm[kk](dev_x[kk])
                 if kk in ("o", "down") and world > 1:
                     y = y.float()
-                    dist.all_reduce(y)
+                    exchange(y)
                 last[kk] = y
 
     with torch.cuda.stream(stream):

@@ -42,6 +42,12 @@ _PROTOS = {
     "fbfp_gemv_resident": (_c_int, [_vp, _c_int, _c_i64, _c_i64, _vp, _vp, _vp, _c_i64, _c_i64, _c_i64,
                                     _c_i64, _vp, _vp, _vp, _c_int, _vp, _c_int, _c_i64, _vp, _vp]),
     "fbfp_stream_fence": (_c_int, [_vp]),
+    "fbfp_allreduce_ipc_handle_bytes": (_c_i64, []),
+    "fbfp_allreduce_create": (_c_int, [_c_int, _c_int, _c_i64, _vp, _vp]),
+    "fbfp_allreduce_open_peer": (_c_int, [_vp, _c_int, _vp]),
+    "fbfp_allreduce_sum_f32": (_c_int, [_vp, _vp, _c_i64, _vp]),
+    "fbfp_allreduce_check": (_c_int, [_vp, _vp]),
+    "fbfp_allreduce_destroy": (_c_int, [_vp]),
     "fbfp_gemm_prefill": (_c_int, [_vp, _c_int, _c_i64, _c_i64, _vp, _vp, _vp, _c_i64, _c_i64, _c_i64,
                                    _c_i64, _vp, _vp, _vp, _c_int, _vp, _c_int, _c_i64, _vp, _vp]),
     "fbfp_compress_scratch_bytes": (_c_i64, [_c_i64, _c_i64, _c_i64, _c_i64]),

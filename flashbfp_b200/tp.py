@@ -74,12 +74,62 @@ def slice_packed(pw: packed.PackedWeight, name: str, rank: int, world: int,
     return packed.shard_cols(pw, c0 // 16, (c1 + 15) // 16, tiles=tiles)
 
 
-def all_reduce_sum(y: torch.Tensor, group=None) -> torch.Tensor:
-    """Sum of the ranks' fp32 partial outputs (row-parallel exchange), in place."""
+def all_reduce_sum(y: torch.Tensor, group=None, reducer: Optional["NVLinkAllReduce"] = None) -> torch.Tensor:
+    """Sum of the ranks' fp32 partial outputs (row-parallel exchange), in place: through the
+    NVLink peer-memory reducer when one is given, else the process group's all-reduce."""
+    if reducer is not None:
+        return reducer(y)
     import torch.distributed as dist
     if dist.is_available() and dist.is_initialized() and dist.get_world_size(group) > 1:
         dist.all_reduce(y, op=dist.ReduceOp.SUM, group=group)
     return y
+
+
+class NVLinkAllReduce:
+    """One-shot fp32 sum all-reduce over NVLink peer memory (csrc/allreduce.cu) for the
+    row-parallel exchange. Every rank creates one (collectively: the CUDA IPC handles of the
+    ranks' buffers are exchanged through the process group) on its current CUDA device; calls
+    must be made by all ranks in the same order. Capturable in CUDA graphs."""
+
+    def __init__(self, max_elems: int, group=None):
+        import ctypes
+        import torch.distributed as dist
+        from . import _lib
+        self._L = L = _lib.lib()
+        self._lib = _lib
+        self.world = dist.get_world_size(group)
+        self.rank = dist.get_rank(group)
+        self.max_elems = int(max_elems)
+        h = ctypes.c_void_p()
+        ipc = ctypes.create_string_buffer(int(L.fbfp_allreduce_ipc_handle_bytes()))
+        _lib.check(L.fbfp_allreduce_create(self.world, self.rank, self.max_elems, ctypes.byref(h), ipc),
+                   "fbfp_allreduce_create")
+        self._h = h
+        handles = [None] * self.world
+        dist.all_gather_object(handles, bytes(ipc.raw), group=group)
+        for p in range(self.world):
+            if p != self.rank:
+                _lib.check(L.fbfp_allreduce_open_peer(h, p, handles[p]), "fbfp_allreduce_open_peer")
+        dist.barrier(group=group)
+
+    def __call__(self, y: torch.Tensor) -> torch.Tensor:
+        if y.dtype != torch.float32 or not y.is_contiguous():
+            raise ValueError("NVLinkAllReduce sums contiguous fp32 tensors")
+        self._lib.check(self._L.fbfp_allreduce_sum_f32(self._h, self._lib.ptr(y), y.numel(),
+                                                       self._lib.stream_ptr(y.device)),
+                        "fbfp_allreduce_sum_f32")
+        return y
+
+    def check(self, device=None) -> None:
+        """Synchronise and raise if a call gave up waiting for a rank."""
+        dev = device if device is not None else torch.device("cuda", torch.cuda.current_device())
+        self._lib.check(self._L.fbfp_allreduce_check(self._h, self._lib.stream_ptr(dev)),
+                        "fbfp_allreduce_check")
+
+    def close(self) -> None:
+        if self._h:
+            self._L.fbfp_allreduce_destroy(self._h)
+            self._h = None
 
 
 class TPLinear(torch.nn.Module):
@@ -88,9 +138,11 @@ class TPLinear(torch.nn.Module):
     takes the full input, reads its own K range, and returns the complete (all-reduced) output."""
 
     def __init__(self, pw: packed.PackedWeight, name: str, rank: int, world: int, k_full: int,
-                 bias: Optional[torch.Tensor] = None, group=None):
+                 bias: Optional[torch.Tensor] = None, group=None,
+                 reducer: Optional[NVLinkAllReduce] = None):
         super().__init__()
         self.pw, self.mode, self.rank, self.world, self.group = pw, mode_of(name), rank, world, group
+        self.reducer = reducer
         self.k0, self.k1 = input_range(name, k_full, rank, world)
         self.bias = bias
 
@@ -102,7 +154,7 @@ class TPLinear(torch.nn.Module):
             Y = packed_linear(X2, self.pw, self.bias)
         else:
             Y = packed_linear(X2[:, self.k0:self.k1], self.pw, None, torch.float32)
-            all_reduce_sum(Y, self.group)
+            all_reduce_sum(Y, self.group, self.reducer)
             if self.bias is not None:
                 Y = Y + self.bias.float()
             Y = Y.to(X.dtype)

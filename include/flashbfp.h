@@ -147,6 +147,26 @@ int fbfp_gemm_prefill(const void* x, int x_dtype, int64_t m, int64_t ldx,
                       void* y, int y_dtype, int64_t ldy,
                       void* workspace, void* stream);
 
+/* ------------------------------------------------------------------------------------
+ * Tensor-parallel exchange: one-shot fp32 sum all-reduce over NVLink peer memory (plain peer
+ * stores and loads, bounded waits). Replaces the collective of the row-parallel linears (the
+ * reference has no multi-GPU path; this is the exchange of the sharded o/down projections).
+ * One handle per rank and device: fbfp_allreduce_create allocates the rank's buffer and writes
+ * its CUDA IPC handle (fbfp_allreduce_ipc_handle_bytes() bytes) to ipc_handle_out; exchange
+ * the handles between ranks (any host channel) and call fbfp_allreduce_open_peer for every
+ * other rank. fbfp_allreduce_sum_f32 then replaces y[0..n) (n <= max_elems) on every rank with
+ * the sum over ranks, in rank order (bit-identical on every rank); all ranks must make the same
+ * calls in the same order. A wait that gives up (about two seconds: a rank that never
+ * arrives) is reported by fbfp_allreduce_check as FBFP_ERR_TIMEOUT. Graph-capturable.
+ * ---------------------------------------------------------------------------------- */
+int64_t fbfp_allreduce_ipc_handle_bytes(void);
+int fbfp_allreduce_create(int world, int rank, int64_t max_elems, void** handle,
+                          void* ipc_handle_out);
+int fbfp_allreduce_open_peer(void* handle, int peer, const void* ipc_handle);
+int fbfp_allreduce_sum_f32(void* handle, float* y, int64_t n, void* stream);
+int fbfp_allreduce_check(void* handle, void* stream);
+int fbfp_allreduce_destroy(void* handle);
+
 /* fbfp_gemv without a caller workspace. No counterpart in the reference: it exists for
  * callers that cannot allocate device memory — a plugin inside a host application that owns
  * all GPU memory through its own pool and forbids stray cudaMalloc calls, or a thin
