@@ -3,21 +3,23 @@
 // rank, 15 KB at M = 1), a latency-bound size where a collective library's per-call overhead
 // dominates.
 //
-// Each rank owns one device buffer (cudaMalloc, shared with its peers through CUDA IPC):
-//   flags[2][kMaxWorld]  uint32   written by peers: flags[parity][src] = tag of src's last push
-//   epoch, err           uint32   this rank's call counter (device side, so graph replays advance
-//                                 it) and error word
-//   data[2][kMaxWorld][max_elems] fp32: slot [parity][src] holds src's partial of that call
+// Low-latency protocol: every element travels as one aligned 8-byte word {value bits, tag}, so
+// the value and its arrival flag land together (an aligned 8-byte store is seen whole) and no
+// fence or separate flag is needed. Each rank owns one device buffer (cudaMalloc, shared with
+// its peers through CUDA IPC):
+//   epoch, err           uint32  this rank's call counter (device side, so graph replays advance
+//                                it) and error word
+//   slots[2][kMaxWorld][max_elems] {uint32 value bits, uint32 tag}: slot [parity][src] holds
+//                                src's partial of the call with that parity
 // A call with epoch e (parity e & 1, tag e + 1), one CTA:
-//   1. push the local partial into slot [parity][rank] of every rank (peers through NVLink);
-//   2. system-scope fence, then store tag into flags[parity][rank] of every rank (release);
-//   3. wait (bounded) until flags[parity][q] == tag for every rank q (acquire);
-//   4. y = sum over q = 0 .. world-1 of the local slots [parity][q] (fixed order: every rank gets
-//      the same bits);
-//   5. epoch = tag.
-// Reusing a parity two calls later is safe: a rank starts call e + 2 only after it has seen every
-// peer's tag for e + 1, which peers set after finishing call e (stream order). Every wait is
-// bounded: after about two seconds the kernel records an error (fbfp_allreduce_check) and returns.
+//   1. write {y[i], tag} into slot [parity][rank] of every rank (peers through NVLink);
+//   2. for every element and every rank q in rank order, wait (bounded) until the local slot
+//      [parity][q] carries tag, and add its value (fixed order: every rank gets the same bits);
+//   3. epoch = tag.
+// Reusing a parity two calls later is safe: a rank starts call e + 2 only after it has received
+// every peer's words of call e + 1, which peers sent after finishing call e (stream order). Every
+// wait is bounded: after about two seconds the kernel records an error (fbfp_allreduce_check)
+// and the CTA returns.
 #include <cuda_runtime.h>
 #include <stdint.h>
 #include <string.h>
@@ -28,7 +30,7 @@ namespace fbfp {
 
 constexpr int kMaxWorld = 8;
 constexpr int kArThreads = 1024;
-constexpr size_t kArHeader = 512;          // flags (2 x 8 x 4 B), epoch, err; 16-byte aligned data
+constexpr size_t kArHeader = 256;          // epoch, err
 
 struct ArHandle {
   int world = 0, rank = 0, device = 0;
@@ -47,84 +49,62 @@ struct ArArgs {
   uint8_t* self;
 };
 
-__device__ __forceinline__ uint32_t* ar_flags(uint8_t* b) { return reinterpret_cast<uint32_t*>(b); }
-__device__ __forceinline__ uint32_t* ar_epoch(uint8_t* b) { return reinterpret_cast<uint32_t*>(b + 256); }
-__device__ __forceinline__ int32_t* ar_err(uint8_t* b) { return reinterpret_cast<int32_t*>(b + 260); }
-__device__ __forceinline__ float* ar_slot(uint8_t* b, int64_t max_elems, uint32_t par, int src) {
-  return reinterpret_cast<float*>(b + kArHeader) + ((int64_t)par * kMaxWorld + src) * max_elems;
+__device__ __forceinline__ uint32_t* ar_epoch(uint8_t* b) { return reinterpret_cast<uint32_t*>(b); }
+__device__ __forceinline__ int32_t* ar_err(uint8_t* b) { return reinterpret_cast<int32_t*>(b + 4); }
+__device__ __forceinline__ uint2* ar_slot(uint8_t* b, int64_t max_elems, uint32_t par, int src) {
+  return reinterpret_cast<uint2*>(b + kArHeader) + ((int64_t)par * kMaxWorld + src) * max_elems;
 }
 
-__device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {
-  asm volatile("st.release.sys.global.u32 [%0], %1;\n" ::"l"(p), "r"(v) : "memory");
+__device__ __forceinline__ void st_word(uint2* p, uint32_t v, uint32_t tag) {
+  asm volatile("st.relaxed.sys.global.v2.u32 [%0], {%1, %2};\n" ::"l"(p), "r"(v), "r"(tag) : "memory");
 }
-__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
-  uint32_t v;
-  asm volatile("ld.acquire.sys.global.u32 %0, [%1];\n" : "=r"(v) : "l"(p) : "memory");
-  return v;
+__device__ __forceinline__ uint2 ld_word(const uint2* p) {
+  uint2 w;
+  asm volatile("ld.relaxed.sys.global.v2.u32 {%0, %1}, [%2];\n" : "=r"(w.x), "=r"(w.y) : "l"(p) : "memory");
+  return w;
 }
 
 __global__ void __launch_bounds__(kArThreads, 1) allreduce_sum_kernel(const ArArgs a) {
   __shared__ uint32_t s_epoch;
-  __shared__ int s_fail;
+  __shared__ volatile int s_fail;
   const int tid = threadIdx.x;
+  // launched with programmatic stream serialisation: y is written by the previous kernel
+  asm volatile("griddepcontrol.wait;\n" ::: "memory");
   if (tid == 0) { s_epoch = *ar_epoch(a.self); s_fail = 0; }
   __syncthreads();
   const uint32_t e = s_epoch, par = e & 1u, tag = e + 1u;
-  const bool vec = (a.n % 4 == 0) && (a.max_elems % 4 == 0) && ((uintptr_t)a.y % 16 == 0);
-  // 1. push this rank's partial into slot [par][rank] of every rank
+  // 1. push {value, tag} words into slot [par][rank] of every rank
   for (int p = 0; p < a.world; ++p) {
-    float* dst = ar_slot(a.peer[p], a.max_elems, par, a.rank);
-    if (vec) {
-      const float4* src4 = reinterpret_cast<const float4*>(a.y);
-      float4* dst4 = reinterpret_cast<float4*>(dst);
-      for (int64_t i = tid; i < a.n / 4; i += kArThreads) dst4[i] = src4[i];
-    } else {
-      for (int64_t i = tid; i < a.n; i += kArThreads) dst[i] = a.y[i];
-    }
+    uint2* dst = ar_slot(a.peer[p], a.max_elems, par, a.rank);
+    for (int64_t i = tid; i < a.n; i += kArThreads) st_word(dst + i, __float_as_uint(a.y[i]), tag);
   }
-  // 2. make the pushes visible system-wide, then publish the tag to every rank
-  __threadfence_system();
-  __syncthreads();
-  if (tid < a.world) st_release_sys(ar_flags(a.peer[tid]) + par * kMaxWorld + a.rank, tag);
-  // 3. wait for every rank's tag (bounded: about two seconds)
-  if (tid < a.world) {
-    const uint32_t* f = ar_flags(a.self) + par * kMaxWorld + tid;
-    bool ok = false;
-    for (uint32_t it = 0; it < (1u << 25); ++it) {
-      if (ld_acquire_sys(f) == tag) { ok = true; break; }
-      if (it > 1024) __nanosleep(64);
-    }
-    if (!ok) {
-      s_fail = 1;
-      atomicExch(ar_err(a.self), 1 + tid);
-    }
-  }
-  __syncthreads();
-  if (s_fail) return;                       // the epoch stays: the handle reports the error
-  // 4. sum the slots in rank order
-  if (vec) {
-    float4* y4 = reinterpret_cast<float4*>(a.y);
-    for (int64_t i = tid; i < a.n / 4; i += kArThreads) {
-      float4 acc = reinterpret_cast<const float4*>(ar_slot(a.self, a.max_elems, par, 0))[i];
-      for (int q = 1; q < a.world; ++q) {
-        const float4 v = reinterpret_cast<const float4*>(ar_slot(a.self, a.max_elems, par, q))[i];
-        acc.x += v.x; acc.y += v.y; acc.z += v.z; acc.w += v.w;
+  // 2. receive and sum in rank order (each thread its own elements); a wait that gives up sets
+  // s_fail, and every thread then skips to the barrier
+  bool stop = false;
+  for (int64_t i = tid; i < a.n && !stop; i += kArThreads) {
+    float acc = 0.f;
+    for (int q = 0; q < a.world && !stop; ++q) {
+      const uint2* src = ar_slot(a.self, a.max_elems, par, q) + i;
+      uint2 w = ld_word(src);
+      for (uint32_t it = 0; w.y != tag; ++it) {
+        if (it >= (1u << 25) || s_fail) {
+          if (!s_fail) { s_fail = 1; atomicExch(ar_err(a.self), 1 + q); }
+          stop = true;
+          break;
+        }
+        if (it > 256) __nanosleep(64);
+        w = ld_word(src);
       }
-      y4[i] = acc;
+      acc += __uint_as_float(w.x);
     }
-  } else {
-    for (int64_t i = tid; i < a.n; i += kArThreads) {
-      float acc = ar_slot(a.self, a.max_elems, par, 0)[i];
-      for (int q = 1; q < a.world; ++q) acc += ar_slot(a.self, a.max_elems, par, q)[i];
-      a.y[i] = acc;
-    }
+    if (!stop) a.y[i] = acc;
   }
   __syncthreads();
-  if (tid == 0) *ar_epoch(a.self) = tag;    // 5.
+  if (tid == 0 && !s_fail) *ar_epoch(a.self) = tag;    // 3.
 }
 
 static size_t ar_bytes(int64_t max_elems) {
-  return kArHeader + sizeof(float) * 2 * kMaxWorld * (size_t)max_elems;
+  return kArHeader + sizeof(uint2) * 2 * kMaxWorld * (size_t)max_elems;
 }
 
 }  // namespace fbfp
@@ -187,7 +167,19 @@ extern "C" int fbfp_allreduce_sum_f32(void* handle, float* y, int64_t n, void* s
   a.y = y; a.n = n; a.world = h->world; a.rank = h->rank; a.max_elems = h->max_elems;
   for (int p = 0; p < kMaxWorld; ++p) a.peer[p] = p < h->world ? h->peer[p] : nullptr;
   a.self = h->base;
-  allreduce_sum_kernel<<<1, kArThreads, 0, as_stream(stream)>>>(a);
+  // programmatic stream serialisation: the launch overlaps the previous kernel's drain; the
+  // kernel waits for it (griddepcontrol.wait) before reading anything
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(1);
+  cfg.blockDim = dim3(kArThreads);
+  cfg.dynamicSmemBytes = 0;
+  cfg.stream = as_stream(stream);
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  FBFP_CUDA_TRY(cudaLaunchKernelEx(&cfg, allreduce_sum_kernel, a));
   FBFP_LAUNCH_CHECK("allreduce_sum_kernel");
   return FBFP_OK;
 }
@@ -197,10 +189,10 @@ extern "C" int fbfp_allreduce_check(void* handle, void* stream) {
   FBFP_CHECK_ARG(h, "null pointer");
   FBFP_CUDA_TRY(cudaStreamSynchronize(as_stream(stream)));
   int32_t err = 0;
-  FBFP_CUDA_TRY(cudaMemcpy(&err, h->base + 260, sizeof(err), cudaMemcpyDeviceToHost));
+  FBFP_CUDA_TRY(cudaMemcpy(&err, h->base + 4, sizeof(err), cudaMemcpyDeviceToHost));
   if (err) {
     const int32_t zero = 0;
-    FBFP_CUDA_TRY(cudaMemcpy(h->base + 260, &zero, sizeof(zero), cudaMemcpyHostToDevice));
+    FBFP_CUDA_TRY(cudaMemcpy(h->base + 4, &zero, sizeof(zero), cudaMemcpyHostToDevice));
     return set_error(FBFP_ERR_TIMEOUT, "all-reduce: rank %d gave up waiting for rank %d", h->rank,
                      (int)err - 1);
   }
