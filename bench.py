@@ -49,8 +49,9 @@ def parse():
     ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--nccl", action="store_true",
-                    help="row-parallel exchange through NCCL instead of the NVLink peer-memory all-reduce")
+    ap.add_argument("--exchange", choices=("fused", "allreduce", "nccl"), default="fused",
+                    help="row-parallel exchange (tensor parallelism): fused into the GEMV epilogue "
+                         "over NVLink peer memory, a separate NVLink all-reduce kernel, or NCCL")
     ap.add_argument("--no-prefill", action="store_true",
                     help="skip the prefill GEMM and the bf16 cuBLAS decode baseline")
     return ap.parse_args()
@@ -149,8 +150,9 @@ def build_layers(n_layers, rank, world, device):
     return layers, shard_bytes
 
 
-def step_io(layers, m, device, world):
-    """Activation inputs per kind and output buffers per (layer, kind)."""
+def step_io(layers, m, device, fp32_kinds):
+    """Activation inputs per kind and output buffers per (layer, kind) (fp32 for the row-parallel
+    kinds whose partial outputs a separate all-reduce sums)."""
     from flashbfp_b200 import workloads
     L0 = layers[0]
     xs = {kk: workloads.activations(m, L0[kk].k_in, seed=7 + i, device=device)
@@ -159,7 +161,7 @@ def step_io(layers, m, device, world):
     for L in layers:
         o = {}
         for kk in KINDS:
-            rowpar = kk in ("o", "down") and world > 1
+            rowpar = kk in fp32_kinds
             o[kk] = torch.empty(m, L[kk].n_out, dtype=torch.float32 if rowpar else torch.bfloat16,
                                 device=device)
         outs.append(o)
@@ -200,15 +202,26 @@ def run_ours(args):
     _progress(rank, "building layers")
     layers, shard_bytes = build_layers(args.layers, rank, world, device)
     _progress(rank, "layers built")
-    xs, outs = step_io(layers, m, device, world)
+    # row-parallel kinds: exchange fused into the GEMV where the tensor-core kernel takes the
+    # shard, else the GEMV's fp32 partials and a separate all-reduce
+    from flashbfp_b200.linear import fused_shard_eligible
+    rowpar = [kk for kk in ("o", "down") if world > 1]
+    ar_elems = 16 * max(layers[0][kk].n_out for kk in ("o", "down"))
+    fused = {kk for kk in rowpar if args.exchange == "fused" and
+             all(fused_shard_eligible(Ly[kk], ar_elems) for Ly in layers)}
+    if world > 1:                               # every rank takes the same path
+        got = [None] * world
+        dist.all_gather_object(got, sorted(fused))
+        fused = set.intersection(*(set(g) for g in got))
+    xs, outs = step_io(layers, m, device, set(rowpar) - fused)
     from flashbfp_b200 import _lib
     L = _lib.lib()
     ws = {kk: torch.zeros(L.fbfp_gemv_workspace_bytes(16, layers[0][kk].npad), dtype=torch.uint8,
                           device=device) for kk in KINDS}
     reducer = None
-    if world > 1 and not args.nccl:
+    if world > 1 and args.exchange != "nccl":
         from flashbfp_b200.tp import NVLinkAllReduce
-        reducer = NVLinkAllReduce(16 * max(layers[0][kk].n_out for kk in ("o", "down")))
+        reducer = NVLinkAllReduce(ar_elems)
 
     def exchange(y):
         if reducer is not None:
@@ -216,13 +229,19 @@ def run_ours(args):
         else:
             dist.all_reduce(y)
 
+    def launch_one(kk, pw, y):
+        if kk in ("o", "down") and world > 1:
+            if kk in fused:
+                _gemv_fused(L, _lib, xs[kk], pw, y, ws[kk], reducer)
+            else:
+                _gemv(L, _lib, xs[kk], pw, y, ws[kk])
+                exchange(y)
+        else:
+            _gemv(L, _lib, xs[kk], pw, y, ws[kk])
+
     def launch_kind(kk):
         for li, Ly in enumerate(layers):
-            pw = Ly[kk]
-            y = outs[li][kk]
-            _gemv(L, _lib, xs[kk], pw, y, ws[kk])
-            if kk in ("o", "down") and world > 1:
-                exchange(y)
+            launch_one(kk, Ly[kk], outs[li][kk])
 
     stream = torch.cuda.Stream(device)
     stream.wait_stream(torch.cuda.current_stream(device))
@@ -239,10 +258,7 @@ def run_ours(args):
         # programmatic dependent launch
         for li, Ly in enumerate(layers):
             for kk in KINDS:
-                y = outs[li][kk]
-                _gemv(L, _lib, xs[kk], Ly[kk], y, ws[kk])
-                if kk in ("o", "down") and world > 1:
-                    exchange(y)
+                launch_one(kk, Ly[kk], outs[li][kk])
 
     graphs = {}
     for kk in KINDS:                            # per kind: rates and the roofline kernel
@@ -313,7 +329,7 @@ def run_ours(args):
     # ---------------- e2e through the public module API ----------------
     e2e = None
     if not args.no_e2e:
-        e2e = run_e2e(args, layers, xs, stream, device, world, rank, step_bytes, exchange)
+        e2e = run_e2e(args, layers, xs, stream, device, world, rank, step_bytes, exchange, reducer, fused)
 
     prefill = bf16 = compress = None
     if world == 1 and not args.no_prefill:
@@ -347,8 +363,11 @@ def run_ours(args):
                              "down 3840x15360; OABF block 16, 1.5% StudentT(3)x20 outliers)"),
                 "m": m, "layers": args.layers, "parallelism": f"tp{world}",
                 "exchange": (None if world == 1 else
-                             "NCCL all-reduce" if args.nccl else
-                             "one-shot all-reduce over NVLink peer memory (csrc/allreduce.cu)"),
+                             "NCCL all-reduce" if args.exchange == "nccl" else
+                             "one-shot all-reduce kernel over NVLink peer memory (csrc/allreduce.cu)"
+                             if args.exchange == "allreduce" else
+                             "fused into the GEMV epilogue: peer-memory push and ordered sum over "
+                             "NVLink (fbfp_gemv_allreduce) for %s" % (sorted(fused) or "none")),
                 "launches_per_step": 4 * args.layers,
                 "l2": "inputs larger than L2 (%.2f GB packed per step per rank)" % (step_bytes / world / 1e9),
                 "graphs": ("one CUDA graph per step (192 launches in model order, programmatic "
@@ -400,10 +419,20 @@ def _gemv(L, _lib, X, pw, Y, ws):
                            _lib.stream_ptr(X.device)), "fbfp_gemv")
 
 
-def run_e2e(args, layers, xs, stream, device, world, rank, step_bytes, exchange):
+def _gemv_fused(L, _lib, X, pw, Y, ws, reducer):
+    _lib.check(L.fbfp_gemv_allreduce(_lib.ptr(X), _lib.DTYPE_CODE[X.dtype], X.shape[0], X.stride(0),
+                                     _lib.ptr(pw.exps), _lib.ptr(pw.signs), _lib.ptr(pw.payload), pw.n_out,
+                                     pw.k_in, pw.kpad, pw.npad, _lib.ptr(pw.entries if pw.nnz else None),
+                                     _lib.ptr(pw.seg_ptr if pw.nnz else None), None, 0, _lib.ptr(Y),
+                                     _lib.DTYPE_CODE[Y.dtype], Y.stride(0), _lib.ptr(ws), reducer.handle,
+                                     1 if pw.resident else 0, _lib.stream_ptr(X.device)),
+               "fbfp_gemv_allreduce")
+
+
+def run_e2e(args, layers, xs, stream, device, world, rank, step_bytes, exchange, reducer, fused):
     """Public-API step: OABFLinear modules in a CUDA graph; host activations in, outputs out."""
     import torch.distributed as dist
-    from flashbfp_b200.linear import OABFLinear
+    from flashbfp_b200.linear import OABFLinear, packed_linear_allreduce
     mods = []
     for Ly in layers:
         mm = {}
@@ -421,10 +450,13 @@ def run_e2e(args, layers, xs, stream, device, world, rank, step_bytes, exchange)
     def body():
         for mm in mods:
             for kk in KINDS:
-                y = mm[kk](dev_x[kk])
-                if kk in ("o", "down") and world > 1:
-                    y = y.float()
-                    exchange(y)
+                if kk in fused:
+                    y = packed_linear_allreduce(dev_x[kk], mm[kk]._pw, reducer)
+                else:
+                    y = mm[kk](dev_x[kk])
+                    if kk in ("o", "down") and world > 1:
+                        y = y.float()
+                        exchange(y)
                 last[kk] = y
 
     with torch.cuda.stream(stream):

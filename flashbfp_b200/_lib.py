@@ -41,6 +41,9 @@ _PROTOS = {
                                    _c_i64, _vp, _vp, _vp, _c_int, _vp, _c_int, _c_i64, _vp]),
     "fbfp_gemv_resident": (_c_int, [_vp, _c_int, _c_i64, _c_i64, _vp, _vp, _vp, _c_i64, _c_i64, _c_i64,
                                     _c_i64, _vp, _vp, _vp, _c_int, _vp, _c_int, _c_i64, _vp, _vp]),
+    "fbfp_gemv_allreduce": (_c_int, [_vp, _c_int, _c_i64, _c_i64, _vp, _vp, _vp, _c_i64, _c_i64, _c_i64,
+                                     _c_i64, _vp, _vp, _vp, _c_int, _vp, _c_int, _c_i64, _vp, _vp, _c_int,
+                                     _vp]),
     "fbfp_stream_fence": (_c_int, [_vp]),
     "fbfp_allreduce_ipc_handle_bytes": (_c_i64, []),
     "fbfp_allreduce_create": (_c_int, [_c_int, _c_int, _c_i64, _vp, _vp]),

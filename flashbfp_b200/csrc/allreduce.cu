@@ -25,12 +25,13 @@
 #include <string.h>
 
 #include "common.cuh"
+#include "exchange.cuh"
 
 namespace fbfp {
 
-constexpr int kMaxWorld = 8;
+constexpr int kMaxWorld = kXMaxWorld;
 constexpr int kArThreads = 1024;
-constexpr size_t kArHeader = 256;          // epoch, err
+constexpr size_t kArHeader = kXHeader;
 
 struct ArHandle {
   int world = 0, rank = 0, device = 0;
@@ -49,20 +50,13 @@ struct ArArgs {
   uint8_t* self;
 };
 
-__device__ __forceinline__ uint32_t* ar_epoch(uint8_t* b) { return reinterpret_cast<uint32_t*>(b); }
-__device__ __forceinline__ int32_t* ar_err(uint8_t* b) { return reinterpret_cast<int32_t*>(b + 4); }
+__device__ __forceinline__ uint32_t* ar_epoch(uint8_t* b) { return xchg_epoch(b); }
+__device__ __forceinline__ int32_t* ar_err(uint8_t* b) { return xchg_err(b); }
 __device__ __forceinline__ uint2* ar_slot(uint8_t* b, int64_t max_elems, uint32_t par, int src) {
-  return reinterpret_cast<uint2*>(b + kArHeader) + ((int64_t)par * kMaxWorld + src) * max_elems;
+  return xchg_slot(b, max_elems, par, src);
 }
-
-__device__ __forceinline__ void st_word(uint2* p, uint32_t v, uint32_t tag) {
-  asm volatile("st.relaxed.sys.global.v2.u32 [%0], {%1, %2};\n" ::"l"(p), "r"(v), "r"(tag) : "memory");
-}
-__device__ __forceinline__ uint2 ld_word(const uint2* p) {
-  uint2 w;
-  asm volatile("ld.relaxed.sys.global.v2.u32 {%0, %1}, [%2];\n" : "=r"(w.x), "=r"(w.y) : "l"(p) : "memory");
-  return w;
-}
+__device__ __forceinline__ void st_word(uint2* p, uint32_t v, uint32_t tag) { xchg_store(p, v, tag); }
+__device__ __forceinline__ uint2 ld_word(const uint2* p) { return xchg_load(p); }
 
 __global__ void __launch_bounds__(kArThreads, 1) allreduce_sum_kernel(const ArArgs a) {
   __shared__ uint32_t s_epoch;
@@ -141,6 +135,22 @@ extern "C" int fbfp_allreduce_create(int world, int rank, int64_t max_elems, voi
 }
 
 extern "C" int64_t fbfp_allreduce_ipc_handle_bytes() { return (int64_t)sizeof(cudaIpcMemHandle_t); }
+
+namespace fbfp {
+// For the GEMV's fused exchange: the ranks' buffers of a handle whose peers are all open.
+int allreduce_buffers(void* handle, uint8_t** bufs, int* world, int* rank, int64_t* max_elems) {
+  ArHandle* h = reinterpret_cast<ArHandle*>(handle);
+  FBFP_CHECK_ARG(h, "null all-reduce handle");
+  for (int p = 0; p < h->world; ++p) {
+    FBFP_CHECK_ARG(h->opened[p], "peer %d of the all-reduce handle has not been opened", p);
+    bufs[p] = h->peer[p];
+  }
+  *world = h->world;
+  *rank = h->rank;
+  *max_elems = h->max_elems;
+  return FBFP_OK;
+}
+}  // namespace fbfp
 
 extern "C" int fbfp_allreduce_open_peer(void* handle, int peer, const void* ipc_handle) {
   ArHandle* h = reinterpret_cast<ArHandle*>(handle);

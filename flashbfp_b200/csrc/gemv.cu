@@ -344,19 +344,27 @@ extern "C" int fbfp_gemv_check(void* workspace, void* stream) {
   FBFP_CUDA_TRY(cudaStreamSynchronize(st));
   if (h != 0) {
     FBFP_CUDA_TRY(cudaMemsetAsync(errp, 0, sizeof(int32_t), st));
+    if (h >= 32)
+      return set_error(FBFP_ERR_TIMEOUT, "fused exchange: gave up waiting for rank %d", (int)h - 32);
     return set_error(FBFP_ERR_TIMEOUT, "a bounded device-side wait gave up (site %d)", (int)h);
   }
   return FBFP_OK;
 }
 
+namespace fbfp {
+int allreduce_buffers(void* handle, uint8_t** bufs, int* world, int* rank, int64_t* max_elems);
+}
+
 // resident != 0: the packed weights and outlier index were not written by the previous kernel in
 // the stream, so the tcgen05 kernel may fetch its first weight stages before that kernel ends.
+// allreduce != null: the row-parallel exchange through that all-reduce handle is fused into the
+// tcgen05 kernel's epilogue (y = bias + the sum over ranks of their partial products).
 static int gemv_impl(const void* x, int x_dtype, int64_t m, int64_t ldx,
                      const int8_t* exponents, const int16_t* signs, const int32_t* payload,
                      int64_t n_out, int64_t k_in, int64_t kpad, int64_t npad,
                      const uint32_t* entries, const int32_t* seg_ptr, const void* bias,
                      int bias_dtype, void* y, int y_dtype, int64_t ldy, void* workspace,
-                     void* stream, int resident) {
+                     void* stream, int resident, void* allreduce) {
   FBFP_CHECK_ARG(x && exponents && signs && payload && y && workspace, "null pointer");
   FBFP_CHECK_ARG(m >= 1 && m <= 16, "fbfp_gemv needs 1 <= m <= 16 (got %lld)", (long long)m);
   FBFP_CHECK_ARG(dtype_ok(x_dtype), "x_dtype must be f32, bf16 or f16");
@@ -385,7 +393,11 @@ static int gemv_impl(const void* x, int x_dtype, int64_t m, int64_t ldx,
   a.vec = (kb_row % 8 == 0) && ((uintptr_t)payload % 16 == 0) && ((uintptr_t)signs % 16 == 0) &&
           ((uintptr_t)exponents % 8 == 0);
   cudaStream_t st = as_stream(stream);
-  if (gemv_tc_eligible(m, kb_row, k_in, x_dtype, ldx, x, payload, signs, exponents)) {
+  const bool tc = gemv_tc_eligible(m, kb_row, k_in, x_dtype, ldx, x, payload, signs, exponents);
+  FBFP_CHECK_ARG(tc || !allreduce,
+                 "the fused exchange needs the tensor-core GEMV: bf16 x, 16-byte aligned operands, "
+                 "kpad a multiple of 256, k_in and ldx multiples of 8");
+  if (tc) {
     TcArgs t;
     t.x = x; t.x_dtype = x_dtype; t.m = (int)m; t.ldx = ldx;
     t.ex = exponents; t.sg = reinterpret_cast<const uint16_t*>(signs);
@@ -397,6 +409,14 @@ static int gemv_impl(const void* x, int x_dtype, int64_t m, int64_t ldx,
     t.n_stages = (int)(kb_row / kStageKb);
     t.total_units = ((npad + kGroupRows - 1) / kGroupRows) * t.n_stages;
     t.early_weights = resident ? 1 : 0;
+    t.world = 1; t.rank = 0; t.xmax = 0; t.exit_count = errp + 1;
+    for (int p = 0; p < 8; ++p) t.xbuf[p] = nullptr;
+    if (allreduce) {
+      int rc = allreduce_buffers(allreduce, t.xbuf, &t.world, &t.rank, &t.xmax);
+      if (rc != FBFP_OK) return rc;
+      FBFP_CHECK_ARG(m * n_out <= t.xmax, "m * n_out = %lld exceeds the all-reduce handle's %lld elements",
+                     (long long)(m * n_out), (long long)t.xmax);
+    }
     return launch_gemv_tc(t, st);
   }
   const dim3 grid((unsigned)((npad + kRowsPerCta - 1) / kRowsPerCta), (unsigned)n_chunks);
@@ -421,7 +441,7 @@ extern "C" int fbfp_gemv(const void* x, int x_dtype, int64_t m, int64_t ldx,
                          int bias_dtype, void* y, int y_dtype, int64_t ldy, void* workspace,
                          void* stream) {
   return gemv_impl(x, x_dtype, m, ldx, exponents, signs, payload, n_out, k_in, kpad, npad, entries,
-                   seg_ptr, bias, bias_dtype, y, y_dtype, ldy, workspace, stream, 0);
+                   seg_ptr, bias, bias_dtype, y, y_dtype, ldy, workspace, stream, 0, nullptr);
 }
 
 extern "C" int fbfp_gemv_resident(const void* x, int x_dtype, int64_t m, int64_t ldx,
@@ -431,7 +451,19 @@ extern "C" int fbfp_gemv_resident(const void* x, int x_dtype, int64_t m, int64_t
                                   int bias_dtype, void* y, int y_dtype, int64_t ldy, void* workspace,
                                   void* stream) {
   return gemv_impl(x, x_dtype, m, ldx, exponents, signs, payload, n_out, k_in, kpad, npad, entries,
-                   seg_ptr, bias, bias_dtype, y, y_dtype, ldy, workspace, stream, 1);
+                   seg_ptr, bias, bias_dtype, y, y_dtype, ldy, workspace, stream, 1, nullptr);
+}
+
+extern "C" int fbfp_gemv_allreduce(const void* x, int x_dtype, int64_t m, int64_t ldx,
+                                   const int8_t* exponents, const int16_t* signs,
+                                   const int32_t* payload, int64_t n_out, int64_t k_in, int64_t kpad,
+                                   int64_t npad, const uint32_t* entries, const int32_t* seg_ptr,
+                                   const void* bias, int bias_dtype, void* y, int y_dtype, int64_t ldy,
+                                   void* workspace, void* allreduce, int resident, void* stream) {
+  FBFP_CHECK_ARG(allreduce, "null all-reduce handle");
+  return gemv_impl(x, x_dtype, m, ldx, exponents, signs, payload, n_out, k_in, kpad, npad, entries,
+                   seg_ptr, bias, bias_dtype, y, y_dtype, ldy, workspace, stream, resident ? 1 : 0,
+                   allreduce);
 }
 
 namespace fbfp {

@@ -35,6 +35,7 @@
 #include "tc_args.h"
 #include "tc_host.h"
 #include "dq_pair.cuh"
+#include "exchange.cuh"
 
 namespace fbfp {
 using namespace sm100;
@@ -71,9 +72,13 @@ constexpr size_t kSegOff = kSoutOff;
 // fp32 (one lane owns each row, so plain stores)
 constexpr size_t kOaccOff = kSegOff + (kSegCache + 8) * sizeof(int32_t);
 constexpr size_t kOaccBytes = 2 * 16 * 128 * sizeof(float);
-constexpr size_t kBarOff = kOaccOff + kOaccBytes;
+// finished values of the rows an epilogue warp owns, [4 warps][16 tokens][32 lanes] fp32
+constexpr size_t kXvOff = kOaccOff + kOaccBytes;
+constexpr size_t kXvBytes = 4 * 16 * 32 * sizeof(float);
+constexpr size_t kBarOff = kXvOff + kXvBytes;
 constexpr int kNumBars = 2 * kStages + 2 * kASlots + 8;
 constexpr size_t kSmemBytes = kBarOff + kNumBars * 8 + 16 + 1024;   // + alignment slack
+static_assert(kSmemBytes <= 232448, "exceeds the 227 KB of shared memory a CTA may opt in to");
 }  // namespace tc
 
 struct TcMaps {
@@ -86,6 +91,7 @@ struct TcShared {
   int32_t* seg;          // seg_ptr[u0 .. u0 + kSegCache]
   uint64_t *full, *empty, *afull, *aempty, *dfull, *dempty, *ofull, *oempty;
   float* oacc;           // [2][16][128]
+  float* xv;             // [4][16][32]
   uint32_t* tmem_slot;
   volatile int* abort_flag;
 };
@@ -107,6 +113,7 @@ __device__ __forceinline__ TcShared tc_shared(uint8_t* smem_raw) {
   S.ofull = S.dempty + 2;
   S.oempty = S.ofull + 2;
   S.oacc = reinterpret_cast<float*>(smem + tc::kOaccOff);
+  S.xv = reinterpret_cast<float*>(smem + tc::kXvOff);
   S.tmem_slot = reinterpret_cast<uint32_t*>(S.oempty + 2);
   S.abort_flag = reinterpret_cast<volatile int*>(S.tmem_slot + 1);
   return S;
@@ -366,11 +373,82 @@ __device__ void tc_outliers(const TcShared& S, const TcArgs& a, int64_t u0, int6
   }
 }
 
+__device__ __forceinline__ uint64_t global_ns() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
+// Waits (bounded: about four seconds, or until another role of the CTA aborts) for the word of
+// this call's tag at `src` and returns its value in *v.
+__device__ __forceinline__ bool tc_xchg_wait(const TcShared& S, const TcArgs& a, const uint2* src,
+                                             uint32_t tag, int code, float* v) {
+  uint2 w = xchg_load(src);
+  uint64_t t0 = 0;
+  for (uint32_t it = 1; w.y != tag; ++it) {
+    if ((it & 63) == 0) {
+      if (*S.abort_flag) return false;
+      const uint64_t now = global_ns();
+      if (t0 == 0) {
+        t0 = now;
+      } else if (now - t0 > 4000000000ull) {
+        *S.abort_flag = 1;
+        atomicExch(a.err, code);
+        return false;
+      }
+    }
+    if (it > 128) __nanosleep(128);
+    w = xchg_load(src);
+  }
+  *v = __uint_as_float(w.x);
+  return true;
+}
+
+// Final values of output row `row` for the m tokens; the lane's values v[t] sit at xv[32 t].
+// One rank: y = v + bias. Row-parallel exchange (world > 1): push v to every peer's slot
+// [par][rank], then y = bias + the sum in rank order of every rank's v (identical bits on all
+// ranks). Returns false if a wait gave up.
+__device__ __forceinline__ bool tc_finish_row(const TcShared& S, const TcArgs& a, int64_t row,
+                                              const float* xv, uint32_t tag, uint32_t par) {
+  const volatile float* v = xv;
+  const int m = a.m;
+  const float bv = a.bias ? load_as_float(a.bias, a.bias_dtype, row) : 0.f;
+  if (a.world > 1) {
+    for (int p = 0; p < a.world; ++p) {
+      if (p == a.rank) continue;
+      uint2* dst = xchg_slot(a.xbuf[p], a.xmax, par, a.rank) + row;
+      for (int t = 0; t < m; ++t) xchg_store(dst + (int64_t)t * a.n_out, __float_as_uint(v[32 * t]), tag);
+    }
+  }
+  for (int t = 0; t < m; ++t) {
+    float acc = v[32 * t];
+    if (a.world > 1) {
+      acc = 0.f;
+      for (int q = 0; q < a.world; ++q) {
+        float w = v[32 * t];
+        if (q != a.rank &&
+            !tc_xchg_wait(S, a, xchg_slot(a.xbuf[a.rank], a.xmax, par, q) + (int64_t)t * a.n_out + row,
+                          tag, 32 + q, &w))
+          return false;
+        acc += w;
+      }
+    }
+    store_from_float(a.y, a.y_dtype, (int64_t)t * a.ldy + row, acc + bv);
+  }
+  return true;
+}
+
 // Epilogue warpgroup (warp w reads tensor-memory lane quarter w % 4, i.e. rows 32q .. 32q+31 of
 // the group): per segment it drains the accumulator (all m tokens), adds the dequantisers'
-// outlier partial sums, then either writes y directly (the CTA covered the whole row group) or
-// adds into the fp32 workspace; a counter per (row group, quarter) collects the units of all
-// CTAs and the warp that completes it writes y and returns the workspace rows to zero.
+// outlier partial sums, then either finishes the rows directly (the CTA covered the whole row
+// group) or adds into the fp32 workspace; a counter per (row group, quarter) collects the units
+// of all CTAs and the warp that completes it finishes the rows and returns the workspace rows to
+// zero. Finishing a row writes y, after the exchange with the other ranks when it is fused in.
+//
+// The exchange cannot deadlock: all CTAs of the grid are resident (one per SM), every rank
+// finishes every row group, and a CTA finishes its row groups in increasing order, so on every
+// rank each contribution to the lowest row group any CTA waits on is either made or comes from a
+// CTA that is not waiting (ranks may split K, and so their units, differently).
 __device__ void tc_epilogue(const TcShared& S, const TcArgs& a, int64_t u0, int64_t u1, uint32_t tmem) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int q4 = warp & 3;
@@ -379,6 +457,13 @@ __device__ void tc_epilogue(const TcShared& S, const TcArgs& a, int64_t u0, int6
   const int m = a.m;
   const float inv15 = 1.0f / 15.0f;
   grid_dependency_wait();                 // the workspace and y may still be in use before this
+  float* xv = S.xv + q4 * 16 * 32 + lane;  // this lane's finished values, one per token
+  uint32_t tag = 0, par = 0;
+  if (a.world > 1) {                      // this call's exchange epoch (advanced at kernel exit)
+    const uint32_t e = *reinterpret_cast<volatile uint32_t*>(xchg_epoch(a.xbuf[a.rank]));
+    par = e & 1u;
+    tag = e + 1u;
+  }
   int64_t seg = 0;
   for (int64_t u = u0; u < u1; ++seg) {
     const int64_t rg = u / a.n_stages;
@@ -410,12 +495,14 @@ __device__ void tc_epilogue(const TcShared& S, const TcArgs& a, int64_t u0, int6
     }
     const bool whole = seg_begin == rg * a.n_stages && seg_end == (rg + 1) * a.n_stages;
     if (whole) {
+      bool ok = true;
       if (rvalid && row < a.n_out) {
-        const float bv = a.bias ? load_as_float(a.bias, a.bias_dtype, row) : 0.f;
 #pragma unroll
         for (int t = 0; t < 16; ++t)
-          if (t < m) store_from_float(a.y, a.y_dtype, (int64_t)t * a.ldy + row, val[t] + bv);
+          if (t < m) xv[32 * t] = val[t];
+        ok = tc_finish_row(S, a, row, xv, tag, par);
       }
+      if (!__all_sync(0xffffffffu, ok)) return;
       continue;
     }
     if (rvalid) {
@@ -433,17 +520,18 @@ __device__ void tc_epilogue(const TcShared& S, const TcArgs& a, int64_t u0, int6
     old = __shfl_sync(0xffffffffu, old, 0);
     if (old + units == a.n_stages) {
       __threadfence();
+      bool ok = true;
       if (rvalid) {
-        const float bv = (a.bias && row < a.n_out) ? load_as_float(a.bias, a.bias_dtype, row) : 0.f;
         for (int t = 0; t < m; ++t) {
           float* wp = a.ws + (int64_t)t * a.npad + row;
-          const float v = __ldcg(wp);
+          xv[32 * t] = __ldcg(wp);
           __stcg(wp, 0.f);
-          if (row < a.n_out) store_from_float(a.y, a.y_dtype, (int64_t)t * a.ldy + row, v + bv);
         }
+        if (row < a.n_out) ok = tc_finish_row(S, a, row, xv, tag, par);
       }
       __syncwarp();
       if (lane == 0) a.counters[rg * 4 + q4] = 0;
+      if (!__all_sync(0xffffffffu, ok)) return;
     }
   }
 }
@@ -511,6 +599,16 @@ gemv_tc_kernel(const TcArgs a, const __grid_constant__ TcMaps M) {
     __syncwarp();
     tc_fence_after();
     tmem_dealloc(tmem, tc::kTmemCols);
+  }
+  // fused exchange: the last CTA to finish advances this rank's epoch (every CTA read it at the
+  // start of its epilogue, before the barrier above)
+  if (a.world > 1 && threadIdx.x == 0) {
+    __threadfence();
+    if (atomicAdd(a.exit_count, 1) == (int)gridDim.x - 1) {
+      *a.exit_count = 0;
+      volatile uint32_t* ep = xchg_epoch(a.xbuf[a.rank]);
+      *ep = *ep + 1u;
+    }
   }
 }
 

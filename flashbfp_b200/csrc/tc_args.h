@@ -24,5 +24,11 @@ struct TcArgs {
   int n_stages;          // kb_row / 16
   int64_t total_units;   // ceil(npad/128) * n_stages
   int early_weights;     // 1: fetch the first weight stages before the grid-dependency wait
+  // Row-parallel exchange fused into the epilogue (world > 1): y = bias + the sum over ranks of
+  // their partial outputs, through the ranks' exchange buffers (exchange.cuh).
+  int world, rank;
+  uint8_t* xbuf[8];
+  int64_t xmax;          // elements per (parity, source) slot
+  int32_t* exit_count;   // CTAs of this call that have finished (in the workspace, zero between calls)
 };
 }  // namespace fbfp

@@ -97,6 +97,53 @@ def packed_linear(X: torch.Tensor, pw: PackedWeight, bias: torch.Tensor | None =
     return Y
 
 
+def fused_shard_eligible(pw: PackedWeight, max_elems: int) -> bool:
+    """Whether the tensor-core GEMV takes shard pw (kpad a multiple of 256, k_in of 8, aligned
+    arrays) and 16 x n_out values fit the exchange buffers of ``max_elems`` elements."""
+    return (pw.kpad % 256 == 0 and pw.k_in % 8 == 0 and 16 * pw.n_out <= max_elems
+            and all(t.data_ptr() % 16 == 0 for t in (pw.exps, pw.signs, pw.payload)))
+
+
+def fused_exchange_eligible(X: torch.Tensor, pw: PackedWeight, max_elems: int) -> bool:
+    """Whether ``packed_linear_allreduce`` can run X (at most 16 tokens per launch) on pw: the
+    tensor-core GEMV's operand rules and room for 16 x n_out values in the exchange buffers."""
+    return (X.is_cuda and X.dim() == 2 and X.dtype == torch.bfloat16 and X.stride(1) == 1
+            and X.stride(0) % 8 == 0 and X.data_ptr() % 16 == 0 and fused_shard_eligible(pw, max_elems))
+
+
+def packed_linear_allreduce(X: torch.Tensor, pw: PackedWeight, reducer, bias: torch.Tensor | None = None,
+                            out_dtype: torch.dtype | None = None,
+                            out: torch.Tensor | None = None) -> torch.Tensor:
+    """Row-parallel shard product with the exchange fused into the GEMV (fbfp_gemv_allreduce):
+    every rank of ``reducer`` (an ``NVLinkAllReduce``) calls it with its K slice X and shard pw,
+    and gets Y = bias + the sum over ranks of X_r @ W_r^T, identical on all ranks."""
+    L = _lib.lib()
+    if not fused_exchange_eligible(X, pw, reducer.max_elems):
+        raise ValueError("packed_linear_allreduce: operands not eligible for the fused exchange")
+    M = X.shape[0]
+    out_dtype = out_dtype or X.dtype
+    Y = out if out is not None else torch.empty(M, pw.n_out, dtype=out_dtype, device=X.device)
+    if M == 0:
+        return Y
+    use_out = pw.nnz > 0 and pw.entries is not None
+    entries = pw.entries if use_out else None
+    seg_ptr = pw.seg_ptr if use_out else None
+    bd = _lib.dtype_code(bias.dtype, "bias") if bias is not None else 0
+    xd = _lib.dtype_code(X.dtype, "X")
+    yd = _lib.dtype_code(out_dtype, "Y")
+    ws = gemv_workspace(X.device, pw.npad)
+    st = _lib.stream_ptr(X.device)
+    for m0 in range(0, M, 16):
+        m = min(16, M - m0)
+        _lib.check(L.fbfp_gemv_allreduce(_lib.ptr(X[m0:m0 + m]), xd, m, X.stride(0), _lib.ptr(pw.exps),
+                                         _lib.ptr(pw.signs), _lib.ptr(pw.payload), pw.n_out, pw.k_in,
+                                         pw.kpad, pw.npad, _lib.ptr(entries), _lib.ptr(seg_ptr),
+                                         _lib.ptr(bias), bd, _lib.ptr(Y[m0:m0 + m]), yd, Y.stride(0),
+                                         _lib.ptr(ws), reducer.handle, 1 if pw.resident else 0, st),
+                   "fbfp_gemv_allreduce")
+    return Y
+
+
 def oabf_gemm(X: torch.Tensor, dense_payload: Dict) -> torch.Tensor:
     """Dense part of the OABF product, ``X @ deq(W)^T`` in X's dtype (triton_kernel.py:130-195).
 

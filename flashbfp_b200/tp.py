@@ -18,6 +18,10 @@ from . import packed
 
 COLUMN_PARALLEL = ("q_proj", "k_proj", "v_proj", "gate_proj", "up_proj")
 ROW_PARALLEL = ("o_proj", "down_proj")
+# Row-parallel shards split K in whole 256-column stages (16 blocks of 16), the tensor-core
+# GEMV's K unit: down_proj's 15360 columns at TP 8 become 1792/2048-column shards that the
+# tensor-core kernel (and its fused exchange) takes, instead of 1920 that it cannot.
+ROW_K_ALIGN = 256
 
 
 def mode_of(name: str) -> str:
@@ -42,12 +46,12 @@ def split(total: int, rank: int, world: int, align: int = 1) -> Tuple[int, int]:
 
 def weight_slice(W: torch.Tensor, name: str, rank: int, world: int) -> torch.Tensor:
     """This rank's part of W [N, K]: output rows (column-parallel) or a K range in whole
-    16-column blocks (row-parallel)."""
+    256-column stages (row-parallel)."""
     n, k = W.shape
     if mode_of(name) == "column":
         r0, r1 = split(n, rank, world, align=16)
         return W[r0:r1]
-    c0, c1 = split(k, rank, world, align=16)
+    c0, c1 = split(k, rank, world, align=ROW_K_ALIGN)
     return W[:, c0:c1]
 
 
@@ -55,7 +59,7 @@ def input_range(name: str, k: int, rank: int, world: int) -> Tuple[int, int]:
     """Columns of the layer input a row-parallel shard reads ([0, k) for column-parallel)."""
     if mode_of(name) == "column":
         return 0, k
-    return split(k, rank, world, align=16)
+    return split(k, rank, world, align=ROW_K_ALIGN)
 
 
 def compress_shard(W: torch.Tensor, name: str, rank: int, world: int, compressor):
@@ -70,7 +74,7 @@ def slice_packed(pw: packed.PackedWeight, name: str, rank: int, world: int,
     if mode_of(name) == "column":
         r0, r1 = split(pw.n_out, rank, world, align=16)
         return packed.shard_rows(pw, r0, r1 if r1 < pw.n_out else pw.npad, tiles=tiles)
-    c0, c1 = split(pw.k_in, rank, world, align=16)
+    c0, c1 = split(pw.k_in, rank, world, align=ROW_K_ALIGN)
     return packed.shard_cols(pw, c0 // 16, (c1 + 15) // 16, tiles=tiles)
 
 
@@ -112,6 +116,11 @@ class NVLinkAllReduce:
                 _lib.check(L.fbfp_allreduce_open_peer(h, p, handles[p]), "fbfp_allreduce_open_peer")
         dist.barrier(group=group)
 
+    @property
+    def handle(self):
+        """The C-ABI handle (for fbfp_gemv_allreduce)."""
+        return self._h
+
     def __call__(self, y: torch.Tensor) -> torch.Tensor:
         if y.dtype != torch.float32 or not y.is_contiguous():
             raise ValueError("NVLinkAllReduce sums contiguous fp32 tensors")
@@ -143,15 +152,28 @@ class TPLinear(torch.nn.Module):
         super().__init__()
         self.pw, self.mode, self.rank, self.world, self.group = pw, mode_of(name), rank, world, group
         self.reducer = reducer
+        self.fused_max_tokens = 64      # decode sizes: beyond this, prefill GEMM + separate exchange
+        # the fused exchange only if every rank's shard takes it (collective: all ranks agree)
+        self.fused_ok = False
+        if reducer is not None and self.mode == "row":
+            import torch.distributed as dist
+            from .linear import fused_shard_eligible
+            flags = [None] * world
+            dist.all_gather_object(flags, fused_shard_eligible(pw, reducer.max_elems), group=group)
+            self.fused_ok = all(flags)
         self.k0, self.k1 = input_range(name, k_full, rank, world)
         self.bias = bias
 
     def forward(self, X: torch.Tensor) -> torch.Tensor:
-        from .linear import packed_linear
+        from .linear import fused_exchange_eligible, packed_linear, packed_linear_allreduce
         lead = X.shape[:-1]
         X2 = X.reshape(-1, X.shape[-1])
         if self.mode == "column":
             Y = packed_linear(X2, self.pw, self.bias)
+        elif (self.fused_ok and X2.shape[0] <= self.fused_max_tokens
+              and fused_exchange_eligible(X2[:, self.k0:self.k1], self.pw, self.reducer.max_elems)):
+            # exchange fused into the GEMV epilogue: bias added once, after the sum
+            Y = packed_linear_allreduce(X2[:, self.k0:self.k1], self.pw, self.reducer, self.bias, X.dtype)
         else:
             Y = packed_linear(X2[:, self.k0:self.k1], self.pw, None, torch.float32)
             all_reduce_sum(Y, self.group, self.reducer)

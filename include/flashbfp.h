@@ -122,6 +122,27 @@ int fbfp_gemv_resident(const void* x, int x_dtype, int64_t m, int64_t ldx,
                        const void* bias, int bias_dtype,
                        void* y, int y_dtype, int64_t ldy,
                        void* workspace, void* stream);
+/* Row-parallel tensor-parallel GEMV with the exchange fused in: every rank of the all-reduce
+ * handle (fbfp_allreduce_create, all peers opened) calls it on its K slice of the matrix (same
+ * n_out, m and unit split on every rank), and every rank gets
+ *   y[m, n] = bias[n] + sum over ranks r (in rank order) of that rank's x_r @ W_r^T,
+ * identical bits on all ranks. The epilogue that finishes a row pushes the row's fp32 partials
+ * into every peer's exchange buffer over NVLink and sums the peers' partials as they arrive, so
+ * the exchange overlaps the rest of the GEMV and costs no separate launch. Replaces, for the
+ * row-parallel (o, down) shards, packed GEMV + dist.all_reduce of the partial outputs + bias.
+ * Requires the tensor-core GEMV (x bf16, 16-byte aligned operands, kpad a multiple of 256, k_in
+ * and ldx multiples of 8) and m * n_out <= the handle's max_elems. resident: as
+ * fbfp_gemv_resident. A wait that gave up (a peer that never arrives: about four seconds) is
+ * reported by fbfp_gemv_check on the workspace; the handle is unusable after that. The handle's
+ * call counter is shared with fbfp_allreduce_sum_f32, so both may be mixed on one stream, in the
+ * same order on every rank. No counterpart in the reference (single-GPU only). */
+int fbfp_gemv_allreduce(const void* x, int x_dtype, int64_t m, int64_t ldx,
+                        const int8_t* exponents, const int16_t* signs, const int32_t* payload,
+                        int64_t n_out, int64_t k_in, int64_t kpad, int64_t npad,
+                        const uint32_t* entries, const int32_t* seg_ptr,
+                        const void* bias, int bias_dtype,
+                        void* y, int y_dtype, int64_t ldy,
+                        void* workspace, void* allreduce, int resident, void* stream);
 /* Launches an empty kernel on `stream`: placed after the kernels that write a matrix's packed
  * arrays, it makes the matrix resident for fbfp_gemv_resident. No counterpart in the reference. */
 int fbfp_stream_fence(void* stream);
