@@ -50,7 +50,7 @@ constexpr int kThreads = 32 * (kDqWarp0 + kDq);
 constexpr uint32_t kTmemCols = 512, kTmemD = 0, kTmemA = 256;
 constexpr size_t kXOff = (size_t)kWStages * kWStageBytes;
 constexpr size_t kBarOff = kXOff + (size_t)kXSlots * kXSlotBytes;
-constexpr int kNumBars = 2 * kWStages + 2 * kXSlots + 2 * kASlots + 2;
+constexpr int kNumBars = 2 * kWStages + 2 * kXSlots + 2 * kASlots + 3;
 constexpr size_t kSmemBytes = kBarOff + kNumBars * 8 + 16 + 1024;
 static_assert(kWStageBytes % 1024 == 0 && kXOff % 1024 == 0, "swizzled buffers need 1 KB alignment");
 static_assert(kTmemA + kASlots * 32 <= kTmemCols, "tensor memory budget");
@@ -83,6 +83,7 @@ struct PfShared {
   uint8_t* wst;          // weight stages
   uint8_t* xst;          // activation chunks
   uint64_t *wfull, *wempty, *xfull, *xempty, *afull, *aempty, *dfull, *dempty;
+  uint64_t* mtail;       // the MMA thread's last commit (its MMAs have completed)
   uint32_t* tmem_slot;
   volatile int* abort_flag;
 };
@@ -101,7 +102,8 @@ __device__ __forceinline__ PfShared pf_shared(uint8_t* smem_raw) {
   S.aempty = S.afull + pf::kASlots;
   S.dfull = S.aempty + pf::kASlots;
   S.dempty = S.dfull + 1;
-  S.tmem_slot = reinterpret_cast<uint32_t*>(S.dempty + 1);
+  S.mtail = S.dempty + 1;
+  S.tmem_slot = reinterpret_cast<uint32_t*>(S.mtail + 1);
   S.abort_flag = reinterpret_cast<volatile int*>(S.tmem_slot + 1);
   return S;
 }
@@ -172,15 +174,21 @@ __device__ void pf_producer_thread(const PfShared& S, const PfArgs& a, const PfM
       }
     }
   }
-  // wind down: copies in flight must land before the CTA exits
+  // wind down: copies in flight must land before the CTA exits, and, unless the CTA aborted,
+  // the MMA's commit arrivals that release the activation chunks must have landed before the
+  // shared memory is freed
   for (int64_t j = issued_w > pf::kWStages ? issued_w - pf::kWStages : 0; j < issued_w; ++j)
     mbar_wait(&S.wfull[j % pf::kWStages], (uint32_t)(j / pf::kWStages) & 1, 1u << 20);
-  for (int64_t j = issued_x > pf::kXSlots ? issued_x - pf::kXSlots : 0; j < issued_x; ++j)
+  const int64_t x0 = issued_x > pf::kXSlots ? issued_x - pf::kXSlots : 0;
+  for (int64_t j = x0; j < issued_x; ++j)
     mbar_wait(&S.xfull[j % pf::kXSlots], (uint32_t)(j / pf::kXSlots) & 1, 1u << 20);
+  for (int64_t j = x0; j < issued_x && ok; ++j)
+    ok = pf_wait(S, a, &S.xempty[j % pf::kXSlots], (uint32_t)(j / pf::kXSlots) & 1, 9);
 }
 
 // ---------------------------------------------------------------------------------------
-__device__ void pf_mma(const PfShared& S, const PfArgs& a, uint32_t tmem) {
+// Issues the CTA's MMAs; `uses` counts the A-slot uses committed. False if a wait gave up.
+__device__ bool pf_mma_loop(const PfShared& S, const PfArgs& a, uint32_t tmem, int64_t& uses) {
   constexpr uint32_t IDESC = idesc_bf16_f32(128, pf::kBN, false);
   // B: a chunk is 256 token rows of 64 k (128-byte swizzled K-major), token groups of 8 are
   // 1024 B apart; block j of the chunk starts 32 * j bytes in
@@ -190,13 +198,13 @@ __device__ void pf_mma(const PfShared& S, const PfArgs& a, uint32_t tmem) {
   uint32_t xph = 0, aph = 0, dph = 0;
   const uint32_t tD = tmem + pf::kTmemD;
   for (int64_t t = blockIdx.x; t < a.n_tiles; t += gridDim.x) {
-    if (!pf_wait(S, a, S.dempty, dph ^ 1, 3)) return;
+    if (!pf_wait(S, a, S.dempty, dph ^ 1, 3)) return false;
     tc_fence_after();
     uint32_t acc = 0;
     for (int st = 0; st < a.n_stages; ++st) {
       for (int c = 0; c < 4; ++c) {
-        if (!pf_wait(S, a, &S.xfull[xs], xph, 4)) return;
-        if (!pf_wait(S, a, &S.afull[slot], aph, 5)) return;
+        if (!pf_wait(S, a, &S.xfull[xs], xph, 4)) return false;
+        if (!pf_wait(S, a, &S.afull[slot], aph, 5)) return false;
         tc_fence_after();
         const uint32_t tA = tmem + pf::kTmemA + slot * 32;
         const uint64_t db = desc0 + (uint64_t)xs * kSlotDesc;
@@ -207,12 +215,33 @@ __device__ void pf_mma(const PfShared& S, const PfArgs& a, uint32_t tmem) {
         acc = 1;
         mma_commit(&S.aempty[slot]);
         mma_commit(&S.xempty[xs]);
+        ++uses;
         if (++slot == pf::kASlots) { slot = 0; aph ^= 1; }
         if (++xs == pf::kXSlots) { xs = 0; xph ^= 1; }
       }
     }
     mma_commit(S.dfull);
     dph ^= 1;
+  }
+  return true;
+}
+
+__device__ void pf_mma(const PfShared& S, const PfArgs& a, uint32_t tmem) {
+  int64_t uses = 0;
+  const bool ok = pf_mma_loop(S, a, tmem, uses);
+  if (uses > 0) {
+    // every MMA this thread issued completes before the tensor memory is released (also when
+    // the CTA aborts with MMAs in flight)
+    mma_commit(S.mtail);
+    mbar_wait(S.mtail, 0, 1u << 22);
+  }
+  if (ok) {
+    // the commit arrivals on the A-slot barriers land before the shared memory is released:
+    // use t of slot t % kASlots completes that barrier's phase t / kASlots
+    for (int j = 0; j < pf::kASlots && j < uses; ++j) {
+      const int64_t last = j + (uses - 1 - j) / pf::kASlots * pf::kASlots;
+      if (!pf_wait(S, a, &S.aempty[j], (uint32_t)(last / pf::kASlots) & 1, 10)) break;
+    }
   }
 }
 
@@ -331,6 +360,7 @@ prefill_tc_kernel(const PfArgs a, const __grid_constant__ PfMaps M) {
     for (int j = 0; j < pf::kASlots; ++j) { mbar_init(&S.afull[j], 4); mbar_init(&S.aempty[j], 1); }
     mbar_init(S.dfull, 1);
     mbar_init(S.dempty, 4);
+    mbar_init(S.mtail, 1);
     *S.abort_flag = 0;
     fence_mbar_init();
   }

@@ -76,7 +76,7 @@ constexpr size_t kOaccBytes = 2 * 16 * 128 * sizeof(float);
 constexpr size_t kXvOff = kOaccOff + kOaccBytes;
 constexpr size_t kXvBytes = 4 * 16 * 32 * sizeof(float);
 constexpr size_t kBarOff = kXvOff + kXvBytes;
-constexpr int kNumBars = 2 * kStages + 2 * kASlots + 8;
+constexpr int kNumBars = 2 * kStages + 2 * kASlots + 9;
 constexpr size_t kSmemBytes = kBarOff + kNumBars * 8 + 16 + 1024;   // + alignment slack
 static_assert(kSmemBytes <= 232448, "exceeds the 227 KB of shared memory a CTA may opt in to");
 }  // namespace tc
@@ -90,6 +90,7 @@ struct TcShared {
   float* s_out;
   int32_t* seg;          // seg_ptr[u0 .. u0 + kSegCache]
   uint64_t *full, *empty, *afull, *aempty, *dfull, *dempty, *ofull, *oempty;
+  uint64_t* mtail;       // the MMA thread's last commit (its MMAs have completed)
   float* oacc;           // [2][16][128]
   float* xv;             // [4][16][32]
   uint32_t* tmem_slot;
@@ -114,7 +115,8 @@ __device__ __forceinline__ TcShared tc_shared(uint8_t* smem_raw) {
   S.oempty = S.ofull + 2;
   S.oacc = reinterpret_cast<float*>(smem + tc::kOaccOff);
   S.xv = reinterpret_cast<float*>(smem + tc::kXvOff);
-  S.tmem_slot = reinterpret_cast<uint32_t*>(S.oempty + 2);
+  S.mtail = S.oempty + 2;
+  S.tmem_slot = reinterpret_cast<uint32_t*>(S.mtail + 1);
   S.abort_flag = reinterpret_cast<volatile int*>(S.tmem_slot + 1);
   return S;
 }
@@ -200,15 +202,24 @@ __device__ void tc_producer(const TcShared& S, const TcArgs& a, const TcMaps& M,
       tc_issue_x(S, a, M, u, s);
       if (++s == tc::kStages) { s = 0; ph ^= 1; }
     }
-    // wind down: every stage issued so far must have landed before the CTA may exit
-    for (int64_t j = i > tc::kStages ? i - tc::kStages : 0; j < i; ++j)
+    // wind down: every stage issued so far must have landed before the CTA may exit, and,
+    // unless the CTA aborted, every consumer must have released it, so that no asynchronous
+    // arrival (an MMA commit) is still due on a stage barrier when the shared memory is freed
+    const int64_t j0 = i > tc::kStages ? i - tc::kStages : 0;
+    for (int64_t j = j0; j < i; ++j)
       mbar_wait(&S.full[j % tc::kStages], (uint32_t)(j / tc::kStages) & 1, 1u << 20);
+    for (int64_t j = j0; j < i; ++j)
+      if (*S.abort_flag || !mbar_wait(&S.empty[j % tc::kStages], (uint32_t)(j / tc::kStages) & 1, 1u << 22))
+        break;
   }
   __syncwarp();
 }
 
 // ---------------------------------------------------------------------------------------
-__device__ void tc_mma(const TcShared& S, const TcArgs& a, int64_t u0, int64_t u1, uint32_t tmem) {
+// Issues the MMAs of units [u0, u1); `uses` counts the A-slot uses committed. False if a wait
+// gave up (the CTA aborts).
+__device__ bool tc_mma_loop(const TcShared& S, const TcArgs& a, int64_t u0, int64_t u1, uint32_t tmem,
+                            int64_t& uses) {
   constexpr uint32_t IDESC = idesc_bf16_f32(128, 16, false);
   // B: a substage's 4 blocks are one 64-k box of tokens (rows) in 128-byte swizzled K-major
   // layout; token groups of 8 are 1024 B apart; block j of the box starts 32 * j bytes in
@@ -223,14 +234,14 @@ __device__ void tc_mma(const TcShared& S, const TcArgs& a, int64_t u0, int64_t u
     const int64_t rg = u / a.n_stages;
     const int64_t seg_end = min(u1, (rg + 1) * a.n_stages);
     const int d = (int)(seg & 1);
-    if (!tc_wait(S, a, &S.dempty[d], (uint32_t)((seg >> 1) & 1) ^ 1, 2)) return;
+    if (!tc_wait(S, a, &S.dempty[d], (uint32_t)((seg >> 1) & 1) ^ 1, 2)) return false;
     tc_fence_after();
     const uint32_t tD = tmem + tc::kTmemD + d * 16;
     uint32_t acc = 0;
     for (; u < seg_end; ++u) {
       const uint64_t dstage = desc0 + (uint64_t)s * kStageDesc;
       for (int sub = 0; sub < 4; ++sub) {
-        if (!tc_wait(S, a, &S.afull[slot], aph, 3)) return;
+        if (!tc_wait(S, a, &S.afull[slot], aph, 3)) return false;
         tc_fence_after();
         const uint32_t tA = tmem + tc::kTmemA + slot * 32;
         const uint64_t dsub = dstage + (uint64_t)sub * kBoxDesc;
@@ -240,12 +251,33 @@ __device__ void tc_mma(const TcShared& S, const TcArgs& a, int64_t u0, int64_t u
         mma_ts(tD, tA + 24, dsub + 3 * kKbDesc, IDESC, 1);
         acc = 1;
         mma_commit(&S.aempty[slot]);
+        ++uses;
         if (++slot == tc::kASlots) { slot = 0; aph ^= 1; }
       }
       mma_commit(&S.empty[s]);
       if (++s == tc::kStages) s = 0;
     }
     mma_commit(&S.dfull[d]);
+  }
+  return true;
+}
+
+__device__ void tc_mma(const TcShared& S, const TcArgs& a, int64_t u0, int64_t u1, uint32_t tmem) {
+  int64_t uses = 0;
+  const bool ok = tc_mma_loop(S, a, u0, u1, tmem, uses);
+  if (uses > 0) {
+    // every MMA this thread issued completes before the tensor memory is released (also when
+    // the CTA aborts with MMAs in flight)
+    mma_commit(S.mtail);
+    mbar_wait(S.mtail, 0, 1u << 22);
+  }
+  if (ok) {
+    // the commit arrivals on the A-slot barriers land before the shared memory is released:
+    // use t of slot t % kASlots completes that barrier's phase t / kASlots
+    for (int j = 0; j < tc::kASlots && j < uses; ++j) {
+      const int64_t last = j + (uses - 1 - j) / tc::kASlots * tc::kASlots;
+      if (!mbar_wait(&S.aempty[j], (uint32_t)(last / tc::kASlots) & 1, 1u << 22)) break;
+    }
   }
 }
 
@@ -561,6 +593,7 @@ gemv_tc_kernel(const TcArgs a, const __grid_constant__ TcMaps M) {
       mbar_init(&S.ofull[d], 4);                  // the 4 outlier warps
       mbar_init(&S.oempty[d], 4);
     }
+    mbar_init(S.mtail, 1);
     *S.abort_flag = 0;
     fence_mbar_init();
   }
