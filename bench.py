@@ -52,6 +52,8 @@ def parse():
     ap.add_argument("--exchange", choices=("fused", "allreduce", "nccl"), default="fused",
                     help="row-parallel exchange (tensor parallelism): fused into the GEMV epilogue "
                          "over NVLink peer memory, a separate NVLink all-reduce kernel, or NCCL")
+    ap.add_argument("--no-model", action="store_true",
+                    help="skip the full-model decode token step (N = 1 only)")
     ap.add_argument("--no-prefill", action="store_true",
                     help="skip the prefill GEMM and the bf16 cuBLAS decode baseline")
     return ap.parse_args()
@@ -331,6 +333,10 @@ def run_ours(args):
     if not args.no_e2e:
         e2e = run_e2e(args, layers, xs, stream, device, world, rank, step_bytes, exchange, reducer, fused)
 
+    model = None
+    if world == 1 and m == 1 and not args.no_model:
+        model = run_model_decode(layers, device)
+
     prefill = bf16 = compress = None
     if world == 1 and not args.no_prefill:
         prefill = run_prefill(layers, device)
@@ -384,6 +390,7 @@ def run_ours(args):
             },
             "gpu_launches": 4 * args.layers * K,
             "e2e": e2e,
+            "model_decode": model,
             "prefill": prefill,
             "bf16_cublas_decode": bf16,
             "compress": compress,
@@ -565,6 +572,58 @@ def run_compress(device, iters=5):
     return {"workload": f"compress_matrix_device on a {n}x{k} bf16 weight (1.5% StudentT(3) outliers)",
             "ms": round(ms, 4), "input_gbs": round(inp / (ms * 1e-3) / 1e9, 1),
             "algorithmic_gbs": round(alg / (ms * 1e-3) / 1e9, 1), "outliers": int(sp["count"])}
+
+
+def run_model_decode(layers, device, prompt=128, gen=256):
+    """Whole decode tokens of a random-init 12B-class Gemma-3 (the benchmark's OABF layers, 5
+    sliding-window layers of 1024 per global one, 16 query / 8 key-value heads of 256, bf16
+    embedding and lm_head of 262144 x 3840): ``prompt`` tokens fed one per step (not timed), then
+    ``gen`` greedy tokens timed as back-to-back replays of the one-token CUDA graph."""
+    from flashbfp_b200.decode import DecodeLayer, DecoderShape, GemmaDecoder
+    H, I, NH, NKV, HD, V = 3840, 15360, 16, 8, 256, 262144
+    n = len(layers)
+    types = ["full_attention" if (i + 1) % 6 == 0 else "sliding_attention" for i in range(n)]
+    shape = DecoderShape(hidden=H, inter=I, n_heads=NH, n_kv_heads=NKV, head_dim=HD, vocab=V,
+                         layer_types=types, sliding_window=1024, query_pre_attn_scalar=256.0)
+    g = torch.Generator(device=device).manual_seed(11)
+
+    def rnd(*sz, scale):
+        return (scale * torch.randn(*sz, generator=g, device=device)).to(torch.bfloat16)
+
+    dls = [DecodeLayer(qkv=Ly["qkv"], o=Ly["o"], gate_up=Ly["gate_up"], down=Ly["down"],
+                       input_ln=rnd(H, scale=0.1), post_attn_ln=rnd(H, scale=0.1),
+                       pre_ffn_ln=rnd(H, scale=0.1), post_ffn_ln=rnd(H, scale=0.1),
+                       q_norm=rnd(HD, scale=0.1), k_norm=rnd(HD, scale=0.1)) for Ly in layers]
+    dec = GemmaDecoder(shape, dls, rnd(V, H, scale=0.02), rnd(H, scale=0.1), rnd(V, H, scale=0.02),
+                       max_ctx=prompt + gen + 1, device=device)
+    dec.capture()
+    ids = torch.randint(0, V, (prompt,), generator=torch.Generator().manual_seed(5)).tolist()
+    dec.reset(0)
+    for t in ids:
+        with torch.cuda.stream(dec.stream):
+            dec.tok.fill_(t)
+        dec.step()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    dec.stream.synchronize()
+    a.record(dec.stream)
+    for _ in range(gen):
+        dec.step()
+    b.record(dec.stream)
+    dec.check()
+    ms = a.elapsed_time(b) / gen
+    packed = sum(Ly[kk].packed_bytes() for Ly in layers for kk in KINDS)
+    per_token = packed + 2 * V * H + 2 * H        # OABF linears, bf16 lm_head, one embedding row
+    dec.release()
+    del dec
+    torch.cuda.empty_cache()
+    return {"workload": (f"random-init 12B-class Gemma-3 decode: {n} layers (5 sliding-window "
+                         "layers of 1024 per global one), 16 q / 8 kv heads x 256, vocab 262144, "
+                         f"{prompt} prompt tokens then {gen} greedy tokens, batch 1"),
+            "ms_per_token": round(ms, 4), "tokens_per_s": round(1000.0 / ms, 1),
+            "weight_gbs": round(per_token / (ms * 1e-3) / 1e9, 1),
+            "bytes_per_token": per_token,
+            "graph": "one CUDA graph per token: OABF GEMVs, decode.cu kernels, bf16 lm_head, argmax",
+            "lm_head": "uncompressed bf16 262144x3840 through cuBLAS (left alone by the model surgery)"}
 
 
 def run_bf16_decode(device, m=1, n_layers=8, iters=50):

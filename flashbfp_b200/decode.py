@@ -1,0 +1,247 @@
+"""One Gemma-3 decode token on the GPU, replayed from a single CUDA graph.
+
+The linears run as OABF GEMVs (q|k|v and gate|up fused into one launch each); the work between
+them runs in the kernels of csrc/decode.cu: the scaled embedding, the RMSNorms (the post-norm,
+residual add and next pre-norm between a layer's halves in one kernel), q/k RMSNorm with the
+rotary embedding and the KV-cache append, decode attention (GQA, sliding window on the layers
+that have one) and the GeGLU activation. lm_head stays an uncompressed bf16 linear, as in the
+reference, whose model surgery leaves it alone (flash_bfp/model.py:23-28), and the greedy pick
+is an argmax. The token and its position live on the device, so one replay is one token with no
+host work in between.
+
+``GemmaDecoder.from_hf`` takes a Hugging Face Gemma-3 causal LM after ``compress_gemma_model``;
+``GemmaDecoder(...)`` takes the parts directly (used by the benchmark's random-init 12B-class
+model).
+"""
+from __future__ import annotations
+
+from dataclasses import dataclass
+from typing import List, Optional, Sequence
+
+import torch
+
+from . import _lib
+from .linear import packed_linear
+from .packed import PackedWeight, concat_rows
+
+
+@dataclass
+class DecoderShape:
+    hidden: int
+    inter: int
+    n_heads: int
+    n_kv_heads: int
+    head_dim: int
+    vocab: int
+    layer_types: Sequence[str]            # "sliding_attention" / "full_attention" per layer
+    sliding_window: int
+    query_pre_attn_scalar: float
+    rms_norm_eps: float = 1e-6
+    rope_theta_local: float = 10000.0
+    rope_theta_global: float = 1000000.0
+
+
+@dataclass
+class DecodeLayer:
+    qkv: PackedWeight                     # q | k | v rows
+    o: PackedWeight
+    gate_up: PackedWeight                 # gate | up rows
+    down: PackedWeight
+    input_ln: torch.Tensor                # bf16 RMSNorm weights (applied as 1 + w)
+    post_attn_ln: torch.Tensor
+    pre_ffn_ln: torch.Tensor
+    post_ffn_ln: torch.Tensor
+    q_norm: torch.Tensor
+    k_norm: torch.Tensor
+
+
+def rope_tables(theta: float, head_dim: int, max_ctx: int, device) -> tuple:
+    """bf16 cos/sin rows for positions 0..max_ctx-1, computed as the Hugging Face Gemma-3 rotary
+    embedding computes them (fp32 inverse frequencies, fp32 angles, cos/sin, then bf16)."""
+    inv = 1.0 / (theta ** (torch.arange(0, head_dim, 2, dtype=torch.int64).to(torch.float32) / head_dim))
+    pos = torch.arange(max_ctx, dtype=torch.float32, device=device)
+    freqs = pos[:, None] * inv.to(device)[None, :]
+    emb = torch.cat((freqs, freqs), dim=-1)
+    return emb.cos().to(torch.bfloat16).contiguous(), emb.sin().to(torch.bfloat16).contiguous()
+
+
+class GemmaDecoder:
+    def __init__(self, shape: DecoderShape, layers: List[DecodeLayer], embed: torch.Tensor,
+                 final_norm: torch.Tensor, lm_head: torch.Tensor, max_ctx: int, device=None):
+        self.L = _lib.lib()
+        self.shape, self.layers = shape, layers
+        dev = torch.device(device) if device is not None else embed.device
+        self.device = dev
+        s = shape
+        if len(layers) != len(s.layer_types):
+            raise ValueError(f"{len(layers)} layers but {len(s.layer_types)} layer types")
+        if s.head_dim % 8 or s.head_dim > 256 or max_ctx + 8 * s.head_dim > 10000:
+            raise ValueError("head_dim must be a multiple of 8 up to 256, and max_ctx + 8 * head_dim "
+                             "at most 10000")
+        q_rows = (s.n_heads + 2 * s.n_kv_heads) * s.head_dim
+        for i, ly in enumerate(layers):
+            # the fused rows must hold the heads back to back (each part's rows a multiple of 64)
+            if ly.qkv.n_out != q_rows or ly.gate_up.n_out != 2 * s.inter or ly.o.n_out != s.hidden \
+                    or ly.down.n_out != s.hidden:
+                raise ValueError(f"layer {i}: fused row counts do not match the shape "
+                                 f"(q|k|v {ly.qkv.n_out} vs {q_rows}, gate|up {ly.gate_up.n_out} vs "
+                                 f"{2 * s.inter})")
+        self.max_ctx = int(max_ctx)
+        bf = dict(dtype=torch.bfloat16, device=dev)
+        self.embed = embed.to(**bf).contiguous()
+        self.final_norm = final_norm.to(**bf).contiguous()
+        self.lm_head = lm_head.to(**bf).contiguous()
+        self.embed_scale = float(s.hidden) ** 0.5
+        self.scaling = float(s.query_pre_attn_scalar) ** -0.5
+        self.rope = {
+            "sliding_attention": rope_tables(s.rope_theta_local, s.head_dim, self.max_ctx, dev),
+            "full_attention": rope_tables(s.rope_theta_global, s.head_dim, self.max_ctx, dev),
+        }
+        cache = (len(layers), s.n_kv_heads, self.max_ctx, s.head_dim)
+        self.k_cache = torch.zeros(cache, **bf)
+        self.v_cache = torch.zeros(cache, **bf)
+        self.h = torch.zeros(1, s.hidden, **bf)              # residual stream
+        self.x = torch.zeros(1, s.hidden, **bf)              # normalised input of the next linear
+        self.qkv = torch.zeros(1, q_rows, **bf)
+        self.q = torch.zeros(1, s.n_heads * s.head_dim, **bf)
+        self.attn = torch.zeros(1, s.n_heads * s.head_dim, **bf)
+        self.o = torch.zeros(1, s.hidden, **bf)
+        self.gu = torch.zeros(1, 2 * s.inter, **bf)
+        self.act = torch.zeros(1, s.inter, **bf)
+        self.down = torch.zeros(1, s.hidden, **bf)
+        self.logits = torch.zeros(1, s.vocab, **bf)
+        self.tok = torch.zeros(1, dtype=torch.int64, device=dev)
+        self.pos = torch.zeros(1, dtype=torch.int32, device=dev)
+        self.err = torch.zeros(1, dtype=torch.int32, device=dev)
+        self.graph: Optional[torch.cuda.CUDAGraph] = None
+        self.stream = torch.cuda.Stream(dev)
+
+    # -- construction from a Hugging Face Gemma-3 model after compress_gemma_model -----------
+    @classmethod
+    def from_hf(cls, model, max_ctx: int, device=None) -> "GemmaDecoder":
+        cfg = model.config
+        if getattr(cfg, "final_logit_softcapping", None) or getattr(cfg, "attn_logit_softcapping", None):
+            raise NotImplementedError("logit soft-capping is not supported")
+        rope = cfg.rope_parameters
+        shape = DecoderShape(
+            hidden=cfg.hidden_size, inter=cfg.intermediate_size, n_heads=cfg.num_attention_heads,
+            n_kv_heads=cfg.num_key_value_heads, head_dim=cfg.head_dim, vocab=cfg.vocab_size,
+            layer_types=list(cfg.layer_types), sliding_window=int(cfg.sliding_window),
+            query_pre_attn_scalar=float(cfg.query_pre_attn_scalar), rms_norm_eps=float(cfg.rms_norm_eps),
+            rope_theta_local=float(rope["sliding_attention"]["rope_theta"]),
+            rope_theta_global=float(rope["full_attention"]["rope_theta"]))
+        inner = model.model
+        dev = torch.device(device) if device is not None else inner.embed_tokens.weight.device
+        layers = []
+        with torch.cuda.device(dev):
+            for lyr in inner.layers:
+                at, mlp = lyr.self_attn, lyr.mlp
+                layers.append(DecodeLayer(
+                    qkv=concat_rows([at.q_proj.packed, at.k_proj.packed, at.v_proj.packed]),
+                    o=at.o_proj.packed,
+                    gate_up=concat_rows([mlp.gate_proj.packed, mlp.up_proj.packed]),
+                    down=mlp.down_proj.packed,
+                    input_ln=lyr.input_layernorm.weight.data, post_attn_ln=lyr.post_attention_layernorm.weight.data,
+                    pre_ffn_ln=lyr.pre_feedforward_layernorm.weight.data,
+                    post_ffn_ln=lyr.post_feedforward_layernorm.weight.data,
+                    q_norm=at.q_norm.weight.data, k_norm=at.k_norm.weight.data))
+        for ly in layers:
+            for f in ("input_ln", "post_attn_ln", "pre_ffn_ln", "post_ffn_ln", "q_norm", "k_norm"):
+                setattr(ly, f, getattr(ly, f).to(device=dev, dtype=torch.bfloat16).contiguous())
+        return cls(shape, layers, inner.embed_tokens.weight.data, inner.norm.weight.data,
+                   model.lm_head.weight.data, max_ctx, dev)
+
+    # -- one token ---------------------------------------------------------------------------
+    def _linear(self, x: torch.Tensor, pw: PackedWeight, out: torch.Tensor) -> None:
+        packed_linear(x, pw, None, torch.bfloat16, out=out)
+
+    def _enqueue_step(self) -> None:
+        L, s, st = self.L, self.shape, _lib.stream_ptr(self.device)
+        P = _lib.ptr
+        eps = float(s.rms_norm_eps)
+        _lib.check(L.fbfp_embed(P(self.tok), P(self.embed), s.vocab, s.hidden, self.embed_scale, P(self.h),
+                                P(self.err), st), "fbfp_embed")
+        _lib.check(L.fbfp_rmsnorm(P(self.h), P(self.layers[0].input_ln), eps, s.hidden, P(self.x), st),
+                   "fbfp_rmsnorm")
+        for li, ly in enumerate(self.layers):
+            kind = s.layer_types[li]
+            cos_t, sin_t = self.rope[kind]
+            window = s.sliding_window if kind == "sliding_attention" else 0
+            self._linear(self.x, ly.qkv, self.qkv)
+            _lib.check(L.fbfp_qk_rope_cache(P(self.qkv), s.n_heads, s.n_kv_heads, s.head_dim, P(ly.q_norm),
+                                            P(ly.k_norm), eps, P(cos_t), P(sin_t), P(self.pos), self.max_ctx,
+                                            P(self.q), P(self.k_cache[li]), P(self.v_cache[li]), P(self.err), st),
+                       "fbfp_qk_rope_cache")
+            _lib.check(L.fbfp_decode_attention(P(self.q), P(self.k_cache[li]), P(self.v_cache[li]), s.n_heads,
+                                               s.n_kv_heads, s.head_dim, self.max_ctx, P(self.pos), window,
+                                               self.scaling, P(self.attn), st), "fbfp_decode_attention")
+            self._linear(self.attn, ly.o, self.o)
+            _lib.check(L.fbfp_post_residual_norm(P(self.o), P(ly.post_attn_ln), P(self.h), P(ly.pre_ffn_ln), eps,
+                                                 s.hidden, P(self.x), st), "fbfp_post_residual_norm")
+            self._linear(self.x, ly.gate_up, self.gu)
+            _lib.check(L.fbfp_geglu(P(self.gu), s.inter, P(self.act), st), "fbfp_geglu")
+            self._linear(self.act, ly.down, self.down)
+            nxt = self.layers[li + 1].input_ln if li + 1 < len(self.layers) else self.final_norm
+            _lib.check(L.fbfp_post_residual_norm(P(self.down), P(ly.post_ffn_ln), P(self.h), P(nxt), eps,
+                                                 s.hidden, P(self.x), st), "fbfp_post_residual_norm")
+        torch.matmul(self.x, self.lm_head.t(), out=self.logits)          # bf16 lm_head (cuBLAS)
+        self.tok.copy_(torch.argmax(self.logits, dim=-1))
+        _lib.check(L.fbfp_advance_position(P(self.pos), st), "fbfp_advance_position")
+
+    def reset(self, pos: int = 0) -> None:
+        self.pos.fill_(pos)
+        self.err.zero_()
+
+    def capture(self) -> None:
+        """Record one token step as a CUDA graph (after one eager step that sets the kernels up;
+        the position is restored, and the cache rows that step wrote are rewritten later)."""
+        with torch.cuda.device(self.device), torch.cuda.stream(self.stream):
+            saved_tok, saved_pos = self.tok.clone(), self.pos.clone()
+            self._enqueue_step()
+            self.tok.copy_(saved_tok)
+            self.pos.copy_(saved_pos)
+            self.stream.synchronize()
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g, stream=self.stream):
+                self._enqueue_step()
+        self.graph = g
+
+    def step(self) -> None:
+        """One token: embeds self.tok at position self.pos, leaves the greedy next token in
+        self.tok and the logits in self.logits, and advances self.pos."""
+        with torch.cuda.device(self.device), torch.cuda.stream(self.stream):
+            if self.graph is not None:
+                self.graph.replay()
+            else:
+                self._enqueue_step()
+
+    def check(self) -> None:
+        """Raise if a kernel met an out-of-range token (1) or position (2)."""
+        self.stream.synchronize()
+        e = int(self.err.item())
+        if e:
+            self.err.zero_()
+            raise RuntimeError({1: "token id outside the vocabulary",
+                                2: f"position outside the KV cache ({self.max_ctx})"}.get(e, f"error {e}"))
+
+    def generate(self, prompt: Sequence[int], n_new: int) -> List[int]:
+        """Greedy continuation of ``prompt`` (fed one token per step)."""
+        if len(prompt) + n_new > self.max_ctx:
+            raise ValueError("prompt + new tokens exceed the KV cache")
+        self.reset(0)
+        for t in prompt:
+            with torch.cuda.stream(self.stream):
+                self.tok.fill_(int(t))
+            self.step()
+        out = []
+        for _ in range(n_new):
+            self.stream.synchronize()
+            out.append(int(self.tok.item()))
+            self.step()
+        self.check()
+        return out
+
+    def release(self) -> None:
+        if self.graph is not None:
+            self.graph.reset()
+            self.graph = None
