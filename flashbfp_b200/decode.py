@@ -131,6 +131,12 @@ class GemmaDecoder:
             rope_theta_local=float(rope["sliding_attention"]["rope_theta"]),
             rope_theta_global=float(rope["full_attention"]["rope_theta"]))
         inner = model.model
+        from .linear import OABFLinear
+        for i, lyr in enumerate(inner.layers):
+            mods = (lyr.self_attn.q_proj, lyr.self_attn.k_proj, lyr.self_attn.v_proj, lyr.self_attn.o_proj,
+                    lyr.mlp.gate_proj, lyr.mlp.up_proj, lyr.mlp.down_proj)
+            if not all(isinstance(m, OABFLinear) and m.compressed for m in mods):
+                raise TypeError(f"layer {i} is not compressed: run compress_gemma_model first")
         dev = torch.device(device) if device is not None else inner.embed_tokens.weight.device
         layers = []
         with torch.cuda.device(dev):
