@@ -45,15 +45,15 @@ _PROTOS = {
                                      _c_i64, _vp, _vp, _vp, _c_int, _vp, _c_int, _c_i64, _vp, _vp, _c_int,
                                      _vp]),
     "fbfp_stream_fence": (_c_int, [_vp]),
-    "fbfp_embed": (_c_int, [_vp, _vp, _c_i64, _c_i64, ctypes.c_float, _vp, _vp, _vp]),
-    "fbfp_rmsnorm": (_c_int, [_vp, _vp, ctypes.c_float, _c_i64, _vp, _vp]),
-    "fbfp_post_residual_norm": (_c_int, [_vp, _vp, _vp, _vp, ctypes.c_float, _c_i64, _vp, _vp]),
-    "fbfp_qk_rope_cache": (_c_int, [_vp, _c_i64, _c_i64, _c_i64, _vp, _vp, ctypes.c_float, _vp, _vp, _vp,
-                                    _c_i64, _vp, _vp, _vp, _vp, _vp]),
-    "fbfp_decode_attention": (_c_int, [_vp, _vp, _vp, _c_i64, _c_i64, _c_i64, _c_i64, _vp, _c_i64,
+    "fbfp_embed": (_c_int, [_vp, _c_i64, _vp, _c_i64, _c_i64, ctypes.c_float, _vp, _vp, _vp]),
+    "fbfp_rmsnorm": (_c_int, [_vp, _c_i64, _vp, ctypes.c_float, _c_i64, _vp, _vp]),
+    "fbfp_post_residual_norm": (_c_int, [_vp, _c_i64, _vp, _vp, _vp, ctypes.c_float, _c_i64, _vp, _vp]),
+    "fbfp_qk_rope_cache": (_c_int, [_vp, _c_i64, _c_i64, _c_i64, _c_i64, _vp, _vp, ctypes.c_float, _vp, _vp,
+                                    _vp, _c_i64, _vp, _vp, _vp, _vp, _vp]),
+    "fbfp_decode_attention": (_c_int, [_vp, _c_i64, _vp, _vp, _c_i64, _c_i64, _c_i64, _c_i64, _vp, _c_i64,
                                        ctypes.c_float, _vp, _vp]),
-    "fbfp_geglu": (_c_int, [_vp, _c_i64, _vp, _vp]),
-    "fbfp_advance_position": (_c_int, [_vp, _vp]),
+    "fbfp_geglu": (_c_int, [_vp, _c_i64, _c_i64, _vp, _vp]),
+    "fbfp_advance_position": (_c_int, [_vp, _c_i64, _vp]),
     "fbfp_allreduce_ipc_handle_bytes": (_c_i64, []),
     "fbfp_allreduce_create": (_c_int, [_c_int, _c_int, _c_i64, _vp, _vp]),
     "fbfp_allreduce_open_peer": (_c_int, [_vp, _c_int, _vp]),

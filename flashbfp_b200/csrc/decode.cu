@@ -84,45 +84,53 @@ static cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, s
   return cudaLaunchKernelEx(&cfg, kernel, args...);
 }
 
-// x = bf16(table[tok] * scale) (Gemma's scaled embedding: both operands bf16).
+// Row r of every kernel below is the token at position *pos + r (M rows: a prompt chunk, or
+// one token when decoding).
+
+// x[r] = bf16(table[tok[r]] * scale) (Gemma's scaled embedding: both operands bf16).
 __global__ void embed_kernel(const int64_t* tok, const bf16* table, int64_t vocab, int hidden,
                              float scale, bf16* out, int32_t* err) {
   pdl_prologue();
-  int64_t t = *tok;
+  const int r = blockIdx.y;
+  int64_t t = tok[r];
   if (t < 0 || t >= vocab) {
     if (threadIdx.x == 0 && blockIdx.x == 0) atomicExch(err, 1);
     t = 0;
   }
   const float s = bfr(scale);
+  bf16* o = out + (int64_t)r * hidden;
   for (int d = blockIdx.x * blockDim.x + threadIdx.x; d < hidden; d += gridDim.x * blockDim.x)
-    out[d] = __float2bfloat16_rn(ldb(table + t * hidden + d) * s);
+    o[d] = __float2bfloat16_rn(ldb(table + t * hidden + d) * s);
 }
 
-// y = bf16(x * rsqrt(mean(x^2) + eps) * (1 + w)) for one row of `hidden` values.
+// y[r] = bf16(x[r] * rsqrt(mean(x[r]^2) + eps) * (1 + w)); one CTA per row.
 __global__ void rmsnorm_kernel(const bf16* x, const bf16* w, float eps, int hidden, bf16* y) {
   pdl_prologue();
   extern __shared__ float sh[];                  // hidden values, then 33 for the reduction
   float* red = sh + hidden;
+  const int64_t off = (int64_t)blockIdx.x * hidden;
   float ss = 0.f;
   for (int d = threadIdx.x; d < hidden; d += blockDim.x) {
-    const float v = ldb(x + d);
+    const float v = ldb(x + off + d);
     sh[d] = v;
     ss += v * v;
   }
   const float r = rsqrtf(block_sum(ss, red) / (float)hidden + eps);
   for (int d = threadIdx.x; d < hidden; d += blockDim.x)
-    y[d] = __float2bfloat16_rn(sh[d] * r * (1.f + ldb(w + d)));
+    y[off + d] = __float2bfloat16_rn(sh[d] * r * (1.f + ldb(w + d)));
 }
 
-// Between a layer's halves: h = bf16(resid + post_norm(y)); resid = h; x_next = pre_norm(h).
+// Between a layer's halves, per row: h = bf16(resid + post_norm(y)); resid = h;
+// x_next = pre_norm(h). One CTA per row.
 __global__ void post_residual_pre_kernel(const bf16* y, const bf16* w_post, bf16* resid,
                                          const bf16* w_pre, float eps, int hidden, bf16* x_next) {
   pdl_prologue();
   extern __shared__ float sh[];
   float* red = sh + hidden;
+  const int64_t off = (int64_t)blockIdx.x * hidden;
   float ss = 0.f;
   for (int d = threadIdx.x; d < hidden; d += blockDim.x) {
-    const float v = ldb(y + d);
+    const float v = ldb(y + off + d);
     sh[d] = v;
     ss += v * v;
   }
@@ -130,19 +138,19 @@ __global__ void post_residual_pre_kernel(const bf16* y, const bf16* w_post, bf16
   float hs = 0.f;
   for (int d = threadIdx.x; d < hidden; d += blockDim.x) {
     const float n1 = bfr(sh[d] * r1 * (1.f + ldb(w_post + d)));
-    const float h = bfr(ldb(resid + d) + n1);
-    resid[d] = __float2bfloat16_rn(h);
+    const float h = bfr(ldb(resid + off + d) + n1);
+    resid[off + d] = __float2bfloat16_rn(h);
     sh[d] = h;
     hs += h * h;
   }
   const float r2 = rsqrtf(block_sum(hs, red) / (float)hidden + eps);
   for (int d = threadIdx.x; d < hidden; d += blockDim.x)
-    x_next[d] = __float2bfloat16_rn(sh[d] * r2 * (1.f + ldb(w_pre + d)));
+    x_next[off + d] = __float2bfloat16_rn(sh[d] * r2 * (1.f + ldb(w_pre + d)));
 }
 
-// One CTA per head of the fused q|k|v output: q heads 0..nh-1, then k heads. RMSNorm over the
-// head, rotary embedding at position *pos (cos/sin rows of bf16 tables), then q to q_out and k
-// (with the matching v head, not normalised) appended to the cache at *pos.
+// One CTA per (head, row) of the fused q|k|v rows: q heads 0..nh-1, then k heads. RMSNorm over
+// the head, rotary embedding at the row's position (cos/sin rows of bf16 tables), then q to
+// q_out [row][nh][hd] and k (with the matching v head, not normalised) appended to the cache.
 __global__ void qk_rope_cache_kernel(const bf16* qkv, int nh, int nkv, int hd, const bf16* qnw,
                                      const bf16* knw, float eps, const bf16* cos_t, const bf16* sin_t,
                                      const int32_t* pos_p, int max_ctx, bf16* q_out, bf16* kc, bf16* vc,
@@ -150,14 +158,15 @@ __global__ void qk_rope_cache_kernel(const bf16* qkv, int nh, int nkv, int hd, c
   pdl_prologue();
   extern __shared__ float sh[];                  // hd normalised values, then 33
   float* red = sh + hd;
-  const int head = blockIdx.x;
+  const int head = blockIdx.x, row = blockIdx.y;
   const bool is_q = head < nh;
-  const int p = *pos_p;
+  const int p = *pos_p + row;
   if (p < 0 || p >= max_ctx) {
     if (threadIdx.x == 0) atomicExch(err, 2);
     return;
   }
-  const bf16* x = qkv + (int64_t)head * hd;
+  const int64_t qkv_row = (int64_t)row * (nh + 2 * nkv) * hd;
+  const bf16* x = qkv + qkv_row + (int64_t)head * hd;
   const bf16* w = is_q ? qnw : knw;
   float ss = 0.f;
   for (int d = threadIdx.x; d < hd; d += blockDim.x) {
@@ -172,24 +181,25 @@ __global__ void qk_rope_cache_kernel(const bf16* qkv, int nh, int nkv, int hd, c
   const bf16* cr = cos_t + (int64_t)p * hd;
   const bf16* sr = sin_t + (int64_t)p * hd;
   const int kvh = head - nh;
-  bf16* dst = is_q ? q_out + (int64_t)head * hd : kc + ((int64_t)kvh * max_ctx + p) * hd;
+  bf16* dst = is_q ? q_out + ((int64_t)row * nh + head) * hd : kc + ((int64_t)kvh * max_ctx + p) * hd;
   for (int d = threadIdx.x; d < hd; d += blockDim.x) {
     const float rot = d < half ? -sh[d + half] : sh[d - half];
     const float v = bfr(bfr(sh[d] * ldb(cr + d)) + bfr(rot * ldb(sr + d)));
     dst[d] = __float2bfloat16_rn(v);
   }
   if (!is_q) {
-    const bf16* vsrc = qkv + (int64_t)(nh + nkv + kvh) * hd;
+    const bf16* vsrc = qkv + qkv_row + (int64_t)(nh + nkv + kvh) * hd;
     bf16* vdst = vc + ((int64_t)kvh * max_ctx + p) * hd;
     for (int d = threadIdx.x; d < hd; d += blockDim.x) vdst[d] = vsrc[d];
   }
 }
 
-// One CTA per query head: scores over the cached positions [lo, p] (lo = p - window + 1 for a
-// sliding layer), softmax and the weighted sum of values, all in fp32. A lane owns 8 consecutive
-// dims (one 16-byte load of a cache row; head_dim <= 256, a multiple of 8); warp w takes the
-// positions j = w (mod warps) for both the scores and the weighted sum, whose per-warp partial
-// rows are added in shared memory at the end.
+// One CTA per (query head, row): scores over the cached positions [lo, p] of the row's position
+// p (lo = p - window + 1 for a sliding layer; causal, so a prompt row sees only its prefix),
+// softmax and the weighted sum of values, all in fp32. A lane owns 8 consecutive dims (one
+// 16-byte load of a cache row; head_dim <= 256, a multiple of 8); warp w takes the positions
+// j = w (mod warps) for both the scores and the weighted sum, whose per-warp partial rows are
+// added in shared memory at the end.
 __device__ __forceinline__ void unpack8(const uint4& u, float (&f)[8]) {
   const uint32_t w[4] = {u.x, u.y, u.z, u.w};
 #pragma unroll
@@ -210,15 +220,16 @@ decode_attention_kernel(const bf16* q, const bf16* kc, const bf16* vc, int nh, i
   float* sc = sh;
   float* po = sc + max_ctx;
   float* red = po + nw * hd;
-  const int head = blockIdx.x, kvh = head / (nh / nkv);
-  const int p = *pos_p;
+  const int head = blockIdx.x, row = blockIdx.y, kvh = head / (nh / nkv);
+  const int p = *pos_p + row;
   if (p < 0 || p >= max_ctx) return;             // reported by the cache-append kernel
   const int lo = (window > 0 && p - window + 1 > 0) ? p - window + 1 : 0;
   const int n = p - lo + 1;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const bool act = lane * 8 < hd;
+  const int64_t qo = ((int64_t)row * nh + head) * hd;
   float qv[8];
-  if (act) unpack8(*reinterpret_cast<const uint4*>(q + (int64_t)head * hd + lane * 8), qv);
+  if (act) unpack8(*reinterpret_cast<const uint4*>(q + qo + lane * 8), qv);
   const bf16* kb = kc + ((int64_t)kvh * max_ctx + lo) * hd + lane * 8;
   const bf16* vb = vc + ((int64_t)kvh * max_ctx + lo) * hd + lane * 8;
 #pragma unroll 4
@@ -263,111 +274,126 @@ decode_attention_kernel(const bf16* q, const bf16* kc, const bf16* vc, int nh, i
     float acc = 0.f;
 #pragma unroll
     for (int w = 0; w < nw; ++w) acc += po[w * hd + d];
-    out[(int64_t)head * hd + d] = __float2bfloat16_rn(acc * inv);
+    out[qo + d] = __float2bfloat16_rn(acc * inv);
   }
 }
 
-// out = bf16(bf16(gelu_tanh(gate)) * up) for the fused gate|up output [gate (I) | up (I)].
-__global__ void geglu_kernel(const bf16* gu, int64_t inter, bf16* out) {
+// out[r][i] = bf16(bf16(gelu_tanh(gate[r][i])) * up[r][i]) for the fused rows [gate (I) | up (I)].
+__global__ void geglu_kernel(const bf16* gu, int64_t inter, int64_t total, bf16* out) {
   pdl_prologue();
   const float k0 = 0.7978845608028654f, k1 = 0.044715f;    // sqrt(2/pi), tanh-GELU cubic
-  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < inter;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total;
        i += (int64_t)gridDim.x * blockDim.x) {
-    const float x = ldb(gu + i);
+    const int64_t r = i / inter, c = i - r * inter;
+    const float x = ldb(gu + 2 * inter * r + c);
     const float g = bfr(0.5f * x * (1.f + tanhf(k0 * (x + k1 * x * x * x))));
-    out[i] = __float2bfloat16_rn(g * ldb(gu + inter + i));
+    out[i] = __float2bfloat16_rn(g * ldb(gu + 2 * inter * r + inter + c));
   }
 }
 
-__global__ void advance_kernel(int32_t* pos) {
-  pdl_prologue(); *pos += 1; }
+__global__ void advance_kernel(int32_t* pos, int m) {
+  pdl_prologue();
+  *pos += m;
+}
 
 }  // namespace fbfp
 
 using namespace fbfp;
 
-extern "C" int fbfp_embed(const int64_t* tok, const void* table, int64_t vocab, int64_t hidden, float scale,
-                          void* out, int32_t* err, void* stream) {
+extern "C" int fbfp_embed(const int64_t* tok, int64_t m, const void* table, int64_t vocab, int64_t hidden,
+                          float scale, void* out, int32_t* err, void* stream) {
   FBFP_CHECK_ARG(tok && table && out && err && vocab > 0 && hidden > 0, "bad arguments");
+  FBFP_CHECK_ARG(m >= 1 && m <= 65535, "m must be in [1, 65535]");
   const int blocks = (int)((hidden + 255) / 256);
-  FBFP_CUDA_TRY(launch_pdl(embed_kernel, dim3(blocks), dim3(256), 0, as_stream(stream), tok, reinterpret_cast<const bf16*>(table), vocab,
-                                                      (int)hidden, scale, reinterpret_cast<bf16*>(out), err));
+  FBFP_CUDA_TRY(launch_pdl(embed_kernel, dim3(blocks, (unsigned)m), dim3(256), 0, as_stream(stream), tok,
+                           reinterpret_cast<const bf16*>(table), vocab, (int)hidden, scale,
+                           reinterpret_cast<bf16*>(out), err));
   FBFP_LAUNCH_CHECK("embed_kernel");
   return FBFP_OK;
 }
 
-extern "C" int fbfp_rmsnorm(const void* x, const void* w, float eps, int64_t hidden, void* y, void* stream) {
+extern "C" int fbfp_rmsnorm(const void* x, int64_t m, const void* w, float eps, int64_t hidden, void* y,
+                            void* stream) {
   FBFP_CHECK_ARG(x && w && y && hidden > 0 && hidden <= 12000, "bad arguments (hidden <= 12000)");
+  FBFP_CHECK_ARG(m >= 1 && m <= 65535, "m must be in [1, 65535]");
   const size_t smem = sizeof(float) * ((size_t)hidden + 33);
-  FBFP_CUDA_TRY(launch_pdl(rmsnorm_kernel, dim3(1), dim3(kNormThreads), smem, as_stream(stream), 
-      reinterpret_cast<const bf16*>(x), reinterpret_cast<const bf16*>(w), eps, (int)hidden,
-      reinterpret_cast<bf16*>(y)));
+  FBFP_CUDA_TRY(launch_pdl(rmsnorm_kernel, dim3((unsigned)m), dim3(kNormThreads), smem, as_stream(stream),
+                           reinterpret_cast<const bf16*>(x), reinterpret_cast<const bf16*>(w), eps, (int)hidden,
+                           reinterpret_cast<bf16*>(y)));
   FBFP_LAUNCH_CHECK("rmsnorm_kernel");
   return FBFP_OK;
 }
 
-extern "C" int fbfp_post_residual_norm(const void* y, const void* w_post, void* resid, const void* w_pre,
-                                       float eps, int64_t hidden, void* x_next, void* stream) {
+extern "C" int fbfp_post_residual_norm(const void* y, int64_t m, const void* w_post, void* resid,
+                                       const void* w_pre, float eps, int64_t hidden, void* x_next,
+                                       void* stream) {
   FBFP_CHECK_ARG(y && w_post && resid && w_pre && x_next && hidden > 0 && hidden <= 12000,
                  "bad arguments (hidden <= 12000)");
+  FBFP_CHECK_ARG(m >= 1 && m <= 65535, "m must be in [1, 65535]");
   const size_t smem = sizeof(float) * ((size_t)hidden + 33);
-  FBFP_CUDA_TRY(launch_pdl(post_residual_pre_kernel, dim3(1), dim3(kNormThreads), smem, as_stream(stream), 
-      reinterpret_cast<const bf16*>(y), reinterpret_cast<const bf16*>(w_post), reinterpret_cast<bf16*>(resid),
-      reinterpret_cast<const bf16*>(w_pre), eps, (int)hidden, reinterpret_cast<bf16*>(x_next)));
+  FBFP_CUDA_TRY(launch_pdl(post_residual_pre_kernel, dim3((unsigned)m), dim3(kNormThreads), smem,
+                           as_stream(stream), reinterpret_cast<const bf16*>(y),
+                           reinterpret_cast<const bf16*>(w_post), reinterpret_cast<bf16*>(resid),
+                           reinterpret_cast<const bf16*>(w_pre), eps, (int)hidden,
+                           reinterpret_cast<bf16*>(x_next)));
   FBFP_LAUNCH_CHECK("post_residual_pre_kernel");
   return FBFP_OK;
 }
 
-extern "C" int fbfp_qk_rope_cache(const void* qkv, int64_t nh, int64_t nkv, int64_t hd, const void* q_norm_w,
-                                  const void* k_norm_w, float eps, const void* cos_table, const void* sin_table,
-                                  const int32_t* pos, int64_t max_ctx, void* q_out, void* k_cache, void* v_cache,
-                                  int32_t* err, void* stream) {
+extern "C" int fbfp_qk_rope_cache(const void* qkv, int64_t m, int64_t nh, int64_t nkv, int64_t hd,
+                                  const void* q_norm_w, const void* k_norm_w, float eps, const void* cos_table,
+                                  const void* sin_table, const int32_t* pos, int64_t max_ctx, void* q_out,
+                                  void* k_cache, void* v_cache, int32_t* err, void* stream) {
   FBFP_CHECK_ARG(qkv && q_norm_w && k_norm_w && cos_table && sin_table && pos && q_out && k_cache && v_cache &&
                      err,
                  "null pointer");
   FBFP_CHECK_ARG(nh > 0 && nkv > 0 && nh % nkv == 0 && hd > 0 && hd % 2 == 0 && hd <= 1024 && max_ctx > 0,
                  "bad head shape (nh %lld, nkv %lld, hd %lld)", (long long)nh, (long long)nkv, (long long)hd);
+  FBFP_CHECK_ARG(m >= 1 && m <= 65535, "m must be in [1, 65535]");
   const size_t smem = sizeof(float) * ((size_t)hd + 33);
-  FBFP_CUDA_TRY(launch_pdl(qk_rope_cache_kernel, dim3((unsigned)(nh + nkv)), dim3(128), smem, as_stream(stream), 
-      reinterpret_cast<const bf16*>(qkv), (int)nh, (int)nkv, (int)hd, reinterpret_cast<const bf16*>(q_norm_w),
-      reinterpret_cast<const bf16*>(k_norm_w), eps, reinterpret_cast<const bf16*>(cos_table),
-      reinterpret_cast<const bf16*>(sin_table), pos, (int)max_ctx, reinterpret_cast<bf16*>(q_out),
-      reinterpret_cast<bf16*>(k_cache), reinterpret_cast<bf16*>(v_cache), err));
+  FBFP_CUDA_TRY(launch_pdl(qk_rope_cache_kernel, dim3((unsigned)(nh + nkv), (unsigned)m), dim3(128), smem,
+                           as_stream(stream), reinterpret_cast<const bf16*>(qkv), (int)nh, (int)nkv, (int)hd,
+                           reinterpret_cast<const bf16*>(q_norm_w), reinterpret_cast<const bf16*>(k_norm_w), eps,
+                           reinterpret_cast<const bf16*>(cos_table), reinterpret_cast<const bf16*>(sin_table), pos,
+                           (int)max_ctx, reinterpret_cast<bf16*>(q_out), reinterpret_cast<bf16*>(k_cache),
+                           reinterpret_cast<bf16*>(v_cache), err));
   FBFP_LAUNCH_CHECK("qk_rope_cache_kernel");
   return FBFP_OK;
 }
 
-extern "C" int fbfp_decode_attention(const void* q, const void* k_cache, const void* v_cache, int64_t nh,
-                                     int64_t nkv, int64_t hd, int64_t max_ctx, const int32_t* pos, int64_t window,
-                                     float scaling, void* out, void* stream) {
+extern "C" int fbfp_decode_attention(const void* q, int64_t m, const void* k_cache, const void* v_cache,
+                                     int64_t nh, int64_t nkv, int64_t hd, int64_t max_ctx, const int32_t* pos,
+                                     int64_t window, float scaling, void* out, void* stream) {
   FBFP_CHECK_ARG(q && k_cache && v_cache && pos && out, "null pointer");
   FBFP_CHECK_ARG(nh > 0 && nkv > 0 && nh % nkv == 0 && hd > 0 && hd <= 256 && hd % 8 == 0,
                  "bad head shape (head_dim a multiple of 8, at most 256)");
   FBFP_CHECK_ARG(((uintptr_t)q & 15) == 0 && ((uintptr_t)k_cache & 15) == 0 && ((uintptr_t)v_cache & 15) == 0,
                  "q and the caches must be 16-byte aligned");
   FBFP_CHECK_ARG(max_ctx > 0 && max_ctx + 8 * hd <= 10000, "max_ctx + 8 * head_dim must be <= 10000");
+  FBFP_CHECK_ARG(m >= 1 && m <= 65535, "m must be in [1, 65535]");
   const size_t smem = sizeof(float) * ((size_t)max_ctx + 8 * (size_t)hd + 33);
-  FBFP_CUDA_TRY(launch_pdl(decode_attention_kernel, dim3((unsigned)nh), dim3(kAttnThreads), smem, as_stream(stream), 
-      reinterpret_cast<const bf16*>(q), reinterpret_cast<const bf16*>(k_cache),
-      reinterpret_cast<const bf16*>(v_cache), (int)nh, (int)nkv, (int)hd, (int)max_ctx, pos, (int)window, scaling,
-      reinterpret_cast<bf16*>(out)));
+  FBFP_CUDA_TRY(launch_pdl(decode_attention_kernel, dim3((unsigned)nh, (unsigned)m), dim3(kAttnThreads), smem,
+                           as_stream(stream), reinterpret_cast<const bf16*>(q), reinterpret_cast<const bf16*>(k_cache),
+                           reinterpret_cast<const bf16*>(v_cache), (int)nh, (int)nkv, (int)hd, (int)max_ctx, pos,
+                           (int)window, scaling, reinterpret_cast<bf16*>(out)));
   FBFP_LAUNCH_CHECK("decode_attention_kernel");
   return FBFP_OK;
 }
 
-extern "C" int fbfp_geglu(const void* gate_up, int64_t inter, void* out, void* stream) {
-  FBFP_CHECK_ARG(gate_up && out && inter > 0, "bad arguments");
-  const int64_t want = (inter + 255) / 256;
+extern "C" int fbfp_geglu(const void* gate_up, int64_t m, int64_t inter, void* out, void* stream) {
+  FBFP_CHECK_ARG(gate_up && out && inter > 0 && m >= 1, "bad arguments");
+  const int64_t total = m * inter;
+  const int64_t want = (total + 255) / 256;
   const int blocks = (int)(want < 1184 ? want : 1184);
-  FBFP_CUDA_TRY(launch_pdl(geglu_kernel, dim3(blocks), dim3(256), 0, as_stream(stream), reinterpret_cast<const bf16*>(gate_up), inter,
-                                                      reinterpret_cast<bf16*>(out)));
+  FBFP_CUDA_TRY(launch_pdl(geglu_kernel, dim3(blocks), dim3(256), 0, as_stream(stream),
+                           reinterpret_cast<const bf16*>(gate_up), inter, total, reinterpret_cast<bf16*>(out)));
   FBFP_LAUNCH_CHECK("geglu_kernel");
   return FBFP_OK;
 }
 
-extern "C" int fbfp_advance_position(int32_t* pos, void* stream) {
-  FBFP_CHECK_ARG(pos, "null pointer");
-  FBFP_CUDA_TRY(launch_pdl(advance_kernel, dim3(1), dim3(1), 0, as_stream(stream), pos));
+extern "C" int fbfp_advance_position(int32_t* pos, int64_t m, void* stream) {
+  FBFP_CHECK_ARG(pos && m >= 1 && m <= 65535, "bad arguments");
+  FBFP_CUDA_TRY(launch_pdl(advance_kernel, dim3(1), dim3(1), 0, as_stream(stream), pos, (int)m));
   FBFP_LAUNCH_CHECK("advance_kernel");
   return FBFP_OK;
 }

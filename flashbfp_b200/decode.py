@@ -9,6 +9,10 @@ reference, whose model surgery leaves it alone (flash_bfp/model.py:23-28), and t
 is an argmax. The token and its position live on the device, so one replay is one token with no
 host work in between.
 
+A prompt goes through ``prefill`` as one chunk of rows: the same kernels over M rows at
+consecutive positions (causal attention per row), the linears as M-token launches (the tcgen05
+prefill GEMM once M > 16), and logits for the last row only.
+
 ``GemmaDecoder.from_hf`` takes a Hugging Face Gemma-3 causal LM after ``compress_gemma_model``;
 ``GemmaDecoder(...)`` takes the parts directly (used by the benchmark's random-init 12B-class
 model).
@@ -67,7 +71,8 @@ def rope_tables(theta: float, head_dim: int, max_ctx: int, device) -> tuple:
 
 class GemmaDecoder:
     def __init__(self, shape: DecoderShape, layers: List[DecodeLayer], embed: torch.Tensor,
-                 final_norm: torch.Tensor, lm_head: torch.Tensor, max_ctx: int, device=None):
+                 final_norm: torch.Tensor, lm_head: torch.Tensor, max_ctx: int, device=None,
+                 max_prefill: int = 128):
         self.L = _lib.lib()
         self.shape, self.layers = shape, layers
         dev = torch.device(device) if device is not None else embed.device
@@ -100,17 +105,18 @@ class GemmaDecoder:
         cache = (len(layers), s.n_kv_heads, self.max_ctx, s.head_dim)
         self.k_cache = torch.zeros(cache, **bf)
         self.v_cache = torch.zeros(cache, **bf)
-        self.h = torch.zeros(1, s.hidden, **bf)              # residual stream
-        self.x = torch.zeros(1, s.hidden, **bf)              # normalised input of the next linear
-        self.qkv = torch.zeros(1, q_rows, **bf)
-        self.q = torch.zeros(1, s.n_heads * s.head_dim, **bf)
-        self.attn = torch.zeros(1, s.n_heads * s.head_dim, **bf)
-        self.o = torch.zeros(1, s.hidden, **bf)
-        self.gu = torch.zeros(1, 2 * s.inter, **bf)
-        self.act = torch.zeros(1, s.inter, **bf)
-        self.down = torch.zeros(1, s.hidden, **bf)
+        R = self.max_rows = max(1, int(max_prefill))         # rows of a prompt chunk
+        self.h = torch.zeros(R, s.hidden, **bf)              # residual stream
+        self.x = torch.zeros(R, s.hidden, **bf)              # normalised input of the next linear
+        self.qkv = torch.zeros(R, q_rows, **bf)
+        self.q = torch.zeros(R, s.n_heads * s.head_dim, **bf)
+        self.attn = torch.zeros(R, s.n_heads * s.head_dim, **bf)
+        self.o = torch.zeros(R, s.hidden, **bf)
+        self.gu = torch.zeros(R, 2 * s.inter, **bf)
+        self.act = torch.zeros(R, s.inter, **bf)
+        self.down = torch.zeros(R, s.hidden, **bf)
         self.logits = torch.zeros(1, s.vocab, **bf)
-        self.tok = torch.zeros(1, dtype=torch.int64, device=dev)
+        self.tok = torch.zeros(R, dtype=torch.int64, device=dev)   # ids in; tok[0] = next token
         self.pos = torch.zeros(1, dtype=torch.int32, device=dev)
         self.err = torch.zeros(1, dtype=torch.int32, device=dev)
         self.graph: Optional[torch.cuda.CUDAGraph] = None
@@ -118,7 +124,7 @@ class GemmaDecoder:
 
     # -- construction from a Hugging Face Gemma-3 model after compress_gemma_model -----------
     @classmethod
-    def from_hf(cls, model, max_ctx: int, device=None) -> "GemmaDecoder":
+    def from_hf(cls, model, max_ctx: int, device=None, max_prefill: int = 128) -> "GemmaDecoder":
         cfg = model.config
         if getattr(cfg, "final_logit_softcapping", None) or getattr(cfg, "attn_logit_softcapping", None):
             raise NotImplementedError("logit soft-capping is not supported")
@@ -155,48 +161,68 @@ class GemmaDecoder:
             for f in ("input_ln", "post_attn_ln", "pre_ffn_ln", "post_ffn_ln", "q_norm", "k_norm"):
                 setattr(ly, f, getattr(ly, f).to(device=dev, dtype=torch.bfloat16).contiguous())
         return cls(shape, layers, inner.embed_tokens.weight.data, inner.norm.weight.data,
-                   model.lm_head.weight.data, max_ctx, dev)
+                   model.lm_head.weight.data, max_ctx, dev, max_prefill)
 
     # -- one token ---------------------------------------------------------------------------
     def _linear(self, x: torch.Tensor, pw: PackedWeight, out: torch.Tensor) -> None:
         packed_linear(x, pw, None, torch.bfloat16, out=out)
 
-    def _enqueue_step(self) -> None:
+    def _enqueue(self, m: int) -> None:
+        """Rows 0..m-1 (tokens self.tok[:m] at positions self.pos ..): every layer, then the
+        logits of the last row, the greedy pick into self.tok[0] and pos += m."""
         L, s, st = self.L, self.shape, _lib.stream_ptr(self.device)
         P = _lib.ptr
         eps = float(s.rms_norm_eps)
-        _lib.check(L.fbfp_embed(P(self.tok), P(self.embed), s.vocab, s.hidden, self.embed_scale, P(self.h),
+        h, x, qkv, q, attn = self.h[:m], self.x[:m], self.qkv[:m], self.q[:m], self.attn[:m]
+        o, gu, act, down = self.o[:m], self.gu[:m], self.act[:m], self.down[:m]
+        _lib.check(L.fbfp_embed(P(self.tok), m, P(self.embed), s.vocab, s.hidden, self.embed_scale, P(h),
                                 P(self.err), st), "fbfp_embed")
-        _lib.check(L.fbfp_rmsnorm(P(self.h), P(self.layers[0].input_ln), eps, s.hidden, P(self.x), st),
+        _lib.check(L.fbfp_rmsnorm(P(h), m, P(self.layers[0].input_ln), eps, s.hidden, P(x), st),
                    "fbfp_rmsnorm")
         for li, ly in enumerate(self.layers):
             kind = s.layer_types[li]
             cos_t, sin_t = self.rope[kind]
             window = s.sliding_window if kind == "sliding_attention" else 0
-            self._linear(self.x, ly.qkv, self.qkv)
-            _lib.check(L.fbfp_qk_rope_cache(P(self.qkv), s.n_heads, s.n_kv_heads, s.head_dim, P(ly.q_norm),
+            self._linear(x, ly.qkv, qkv)
+            _lib.check(L.fbfp_qk_rope_cache(P(qkv), m, s.n_heads, s.n_kv_heads, s.head_dim, P(ly.q_norm),
                                             P(ly.k_norm), eps, P(cos_t), P(sin_t), P(self.pos), self.max_ctx,
-                                            P(self.q), P(self.k_cache[li]), P(self.v_cache[li]), P(self.err), st),
+                                            P(q), P(self.k_cache[li]), P(self.v_cache[li]), P(self.err), st),
                        "fbfp_qk_rope_cache")
-            _lib.check(L.fbfp_decode_attention(P(self.q), P(self.k_cache[li]), P(self.v_cache[li]), s.n_heads,
+            _lib.check(L.fbfp_decode_attention(P(q), m, P(self.k_cache[li]), P(self.v_cache[li]), s.n_heads,
                                                s.n_kv_heads, s.head_dim, self.max_ctx, P(self.pos), window,
-                                               self.scaling, P(self.attn), st), "fbfp_decode_attention")
-            self._linear(self.attn, ly.o, self.o)
-            _lib.check(L.fbfp_post_residual_norm(P(self.o), P(ly.post_attn_ln), P(self.h), P(ly.pre_ffn_ln), eps,
-                                                 s.hidden, P(self.x), st), "fbfp_post_residual_norm")
-            self._linear(self.x, ly.gate_up, self.gu)
-            _lib.check(L.fbfp_geglu(P(self.gu), s.inter, P(self.act), st), "fbfp_geglu")
-            self._linear(self.act, ly.down, self.down)
+                                               self.scaling, P(attn), st), "fbfp_decode_attention")
+            self._linear(attn, ly.o, o)
+            _lib.check(L.fbfp_post_residual_norm(P(o), m, P(ly.post_attn_ln), P(h), P(ly.pre_ffn_ln), eps,
+                                                 s.hidden, P(x), st), "fbfp_post_residual_norm")
+            self._linear(x, ly.gate_up, gu)
+            _lib.check(L.fbfp_geglu(P(gu), m, s.inter, P(act), st), "fbfp_geglu")
+            self._linear(act, ly.down, down)
             nxt = self.layers[li + 1].input_ln if li + 1 < len(self.layers) else self.final_norm
-            _lib.check(L.fbfp_post_residual_norm(P(self.down), P(ly.post_ffn_ln), P(self.h), P(nxt), eps,
-                                                 s.hidden, P(self.x), st), "fbfp_post_residual_norm")
-        torch.matmul(self.x, self.lm_head.t(), out=self.logits)          # bf16 lm_head (cuBLAS)
-        self.tok.copy_(torch.argmax(self.logits, dim=-1))
-        _lib.check(L.fbfp_advance_position(P(self.pos), st), "fbfp_advance_position")
+            _lib.check(L.fbfp_post_residual_norm(P(down), m, P(ly.post_ffn_ln), P(h), P(nxt), eps,
+                                                 s.hidden, P(x), st), "fbfp_post_residual_norm")
+        torch.matmul(x[m - 1:m], self.lm_head.t(), out=self.logits)     # bf16 lm_head (cuBLAS)
+        self.tok[:1].copy_(torch.argmax(self.logits, dim=-1))
+        _lib.check(L.fbfp_advance_position(P(self.pos), m, st), "fbfp_advance_position")
+
+    def _enqueue_step(self) -> None:
+        self._enqueue(1)
+
+    def prefill(self, ids: Sequence[int]) -> None:
+        """Run a prompt chunk at positions self.pos .. (at most max_prefill tokens): fills the KV
+        cache, leaves the last row's logits in self.logits, the greedy next token in self.tok[0],
+        and advances self.pos by len(ids)."""
+        m = len(ids)
+        if not 1 <= m <= self.max_rows:
+            raise ValueError(f"a prompt chunk holds 1..{self.max_rows} tokens (got {m})")
+        with torch.cuda.device(self.device), torch.cuda.stream(self.stream):
+            self.tok[:m].copy_(torch.as_tensor(list(ids), dtype=torch.int64), non_blocking=False)
+            self._enqueue(m)
 
     def reset(self, pos: int = 0) -> None:
-        self.pos.fill_(pos)
-        self.err.zero_()
+        """Set the position (and clear the error word) in order with the decoder's stream."""
+        with torch.cuda.device(self.device), torch.cuda.stream(self.stream):
+            self.pos.fill_(pos)
+            self.err.zero_()
 
     def capture(self) -> None:
         """Record one token step as a CUDA graph (after one eager step that sets the kernels up;
@@ -213,8 +239,8 @@ class GemmaDecoder:
         self.graph = g
 
     def step(self) -> None:
-        """One token: embeds self.tok at position self.pos, leaves the greedy next token in
-        self.tok and the logits in self.logits, and advances self.pos."""
+        """One token: embeds self.tok[0] at position self.pos, leaves the greedy next token in
+        self.tok[0] and the logits in self.logits, and advances self.pos."""
         with torch.cuda.device(self.device), torch.cuda.stream(self.stream):
             if self.graph is not None:
                 self.graph.replay()
@@ -226,23 +252,21 @@ class GemmaDecoder:
         self.stream.synchronize()
         e = int(self.err.item())
         if e:
-            self.err.zero_()
+            self.reset(int(self.pos.item()))       # clears the error word on the decoder's stream
             raise RuntimeError({1: "token id outside the vocabulary",
                                 2: f"position outside the KV cache ({self.max_ctx})"}.get(e, f"error {e}"))
 
     def generate(self, prompt: Sequence[int], n_new: int) -> List[int]:
-        """Greedy continuation of ``prompt`` (fed one token per step)."""
+        """Greedy continuation of ``prompt`` (prefilled in chunks of max_prefill tokens)."""
         if len(prompt) + n_new > self.max_ctx:
             raise ValueError("prompt + new tokens exceed the KV cache")
         self.reset(0)
-        for t in prompt:
-            with torch.cuda.stream(self.stream):
-                self.tok.fill_(int(t))
-            self.step()
+        for i in range(0, len(prompt), self.max_rows):
+            self.prefill(prompt[i:i + self.max_rows])
         out = []
         for _ in range(n_new):
             self.stream.synchronize()
-            out.append(int(self.tok.item()))
+            out.append(int(self.tok[0].item()))
             self.step()
         self.check()
         return out

@@ -236,39 +236,42 @@ int fbfp_compress_outliers(const void* w, int w_dtype, int64_t n_out, int64_t k_
                            void* scratch, void* stream);
 
 /* ------------------------------------------------------------------------------------
- * Gemma-3 decode token step around the OABF linears (csrc/decode.cu; no counterpart in the
- * reference, which runs these parts through Hugging Face modules). bf16 activations, one token;
- * the token id (int64) and position (int32) are read from device memory so a whole token step
- * replays from one CUDA graph. RMSNorm: bf16(x * rsqrt(mean(x^2) + eps) * (1 + w)), fp32 inside.
+ * Gemma-3 decoding around the OABF linears (csrc/decode.cu; no counterpart in the reference,
+ * which runs these parts through Hugging Face modules). bf16 activations in rows: m tokens, row r
+ * at position *pos + r (a prompt chunk, or m = 1 per decoded token); token ids (int64) and the
+ * position (int32) are read from device memory, so a token step replays from one CUDA graph.
+ * RMSNorm: bf16(x * rsqrt(mean(x^2) + eps) * (1 + w)), fp32 inside. 1 <= m <= 65535.
  *
- * fbfp_embed: out = bf16(table[*tok] * bf16(scale)); an id outside [0, vocab) sets *err = 1.
- * fbfp_rmsnorm: y = RMSNorm(x; w) over `hidden` (<= 12000) values.
- * fbfp_post_residual_norm: h = bf16(resid + RMSNorm(y; w_post)); resid = h; x_next =
+ * fbfp_embed: out[r] = bf16(table[tok[r]] * bf16(scale)); an id outside [0, vocab) sets *err = 1.
+ * fbfp_rmsnorm: y[r] = RMSNorm(x[r]; w) over `hidden` (<= 12000) values.
+ * fbfp_post_residual_norm: h = bf16(resid[r] + RMSNorm(y[r]; w_post)); resid[r] = h; x_next[r] =
  *   RMSNorm(h; w_pre) (the post-norm, residual add and next pre-norm between a layer's halves).
- * fbfp_qk_rope_cache: on the fused q|k|v row (nh + 2 nkv heads of hd), RMSNorm of every q and k
- *   head, the rotary embedding with the bf16 cos/sin rows at *pos (tables [max_ctx][hd]), q to
- *   q_out [nh][hd], k and v appended to the caches [nkv][max_ctx][hd] at *pos; *pos outside
- *   [0, max_ctx) sets *err = 2 and writes nothing.
- * fbfp_decode_attention: per q head (GQA: kv head = head / (nh / nkv)), softmax(q k^T * scaling)
- *   v over cache positions [lo, *pos] in fp32 (lo = *pos - window + 1 when window > 0, else 0);
- *   hd a multiple of 8 up to 256, max_ctx + 8 hd <= 10000, q and caches 16-byte aligned.
- * fbfp_geglu: out[i] = bf16(bf16(gelu_tanh(gate[i])) * up[i]) for gate_up = [gate | up].
- * fbfp_advance_position: *pos += 1.
+ * fbfp_qk_rope_cache: on each fused q|k|v row (nh + 2 nkv heads of hd), RMSNorm of every q and
+ *   k head, the rotary embedding with the bf16 cos/sin rows at the row's position (tables
+ *   [max_ctx][hd]), q to q_out [m][nh][hd], k and v appended to the caches [nkv][max_ctx][hd];
+ *   a position outside [0, max_ctx) sets *err = 2 and writes nothing for that row.
+ * fbfp_decode_attention: per row and q head (GQA: kv head = head / (nh / nkv)),
+ *   softmax(q k^T * scaling) v over cache positions [lo, p] in fp32, p the row's position and
+ *   lo = p - window + 1 when window > 0, else 0 (causal); hd a multiple of 8 up to 256,
+ *   max_ctx + 8 hd <= 10000, q and caches 16-byte aligned.
+ * fbfp_geglu: out[r][i] = bf16(bf16(gelu_tanh(gate[r][i])) * up[r][i]) for rows [gate | up].
+ * fbfp_advance_position: *pos += m.
  * ---------------------------------------------------------------------------------- */
-int fbfp_embed(const int64_t* tok, const void* table, int64_t vocab, int64_t hidden, float scale,
-               void* out, int32_t* err, void* stream);
-int fbfp_rmsnorm(const void* x, const void* w, float eps, int64_t hidden, void* y, void* stream);
-int fbfp_post_residual_norm(const void* y, const void* w_post, void* resid, const void* w_pre,
-                            float eps, int64_t hidden, void* x_next, void* stream);
-int fbfp_qk_rope_cache(const void* qkv, int64_t nh, int64_t nkv, int64_t hd, const void* q_norm_w,
-                       const void* k_norm_w, float eps, const void* cos_table, const void* sin_table,
-                       const int32_t* pos, int64_t max_ctx, void* q_out, void* k_cache, void* v_cache,
-                       int32_t* err, void* stream);
-int fbfp_decode_attention(const void* q, const void* k_cache, const void* v_cache, int64_t nh,
-                          int64_t nkv, int64_t hd, int64_t max_ctx, const int32_t* pos, int64_t window,
-                          float scaling, void* out, void* stream);
-int fbfp_geglu(const void* gate_up, int64_t inter, void* out, void* stream);
-int fbfp_advance_position(int32_t* pos, void* stream);
+int fbfp_embed(const int64_t* tok, int64_t m, const void* table, int64_t vocab, int64_t hidden,
+               float scale, void* out, int32_t* err, void* stream);
+int fbfp_rmsnorm(const void* x, int64_t m, const void* w, float eps, int64_t hidden, void* y,
+                 void* stream);
+int fbfp_post_residual_norm(const void* y, int64_t m, const void* w_post, void* resid,
+                            const void* w_pre, float eps, int64_t hidden, void* x_next, void* stream);
+int fbfp_qk_rope_cache(const void* qkv, int64_t m, int64_t nh, int64_t nkv, int64_t hd,
+                       const void* q_norm_w, const void* k_norm_w, float eps, const void* cos_table,
+                       const void* sin_table, const int32_t* pos, int64_t max_ctx, void* q_out,
+                       void* k_cache, void* v_cache, int32_t* err, void* stream);
+int fbfp_decode_attention(const void* q, int64_t m, const void* k_cache, const void* v_cache,
+                          int64_t nh, int64_t nkv, int64_t hd, int64_t max_ctx, const int32_t* pos,
+                          int64_t window, float scaling, void* out, void* stream);
+int fbfp_geglu(const void* gate_up, int64_t m, int64_t inter, void* out, void* stream);
+int fbfp_advance_position(int32_t* pos, int64_t m, void* stream);
 
 #ifdef __cplusplus
 }

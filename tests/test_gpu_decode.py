@@ -5,15 +5,17 @@ compressed with compress_gemma_model and run one token at a time through GemmaDe
 reference is the same model whose targeted linears hold the dequantised OABF weights as plain
 bf16 layers, run by Hugging Face over the whole sequence (eager attention, causal and sliding
 masks). Per position the logits agree within 2e-2 relative L2: both sides round to bf16 at every
-module boundary, but not at the same points inside attention, which this runs in fp32. The CUDA
-graph replay reproduces the eager step, and generate() returns in-vocabulary tokens.
+module boundary, but not at the same points inside attention, which this runs in fp32. The same
+holds when the prompt goes through prefill as one chunk (20 rows: the linears take the tcgen05
+prefill GEMM; 5 rows: 16-token GEMV launches) and decoding continues from it. The CUDA graph
+replay reproduces the eager step, and generate() returns in-vocabulary tokens.
 """
 import pytest
 import torch
 
 pytestmark = pytest.mark.gpu
 
-T = 12
+T = 24
 
 
 def _tiny(seed):
@@ -77,7 +79,7 @@ def test_decode_steps_match_hugging_face():
     model = compress_gemma_model(_tiny(1).to(dev, torch.bfloat16), OABFCompressor())
     ref = _dequantised_reference(_tiny(1).to(dev, torch.bfloat16))
     ids = torch.randint(0, 512, (T,), generator=torch.Generator().manual_seed(7)).tolist()
-    dec = GemmaDecoder.from_hf(model, max_ctx=32)
+    dec = GemmaDecoder.from_hf(model, max_ctx=32, max_prefill=20)
     ours = _run(dec, ids)
     check_device_errors(dev)
     with torch.no_grad():
@@ -85,6 +87,25 @@ def test_decode_steps_match_hugging_face():
     for i in range(T):
         rel = ((ours[i] - want[i]).norm() / want[i].norm()).item()
         assert rel <= 2e-2, (i, rel)
+    # prompt chunks through prefill, then decoding continues from the filled cache
+    for n_pre in (20, 5):
+        dec.reset(0)
+        dec.prefill(ids[:n_pre])
+        dec.stream.synchronize()
+        got = [dec.logits[0].float().clone()]
+        for t in ids[n_pre:n_pre + 4]:
+            with torch.cuda.stream(dec.stream):
+                dec.tok.fill_(int(t))
+            dec.step()
+            dec.stream.synchronize()
+            got.append(dec.logits[0].float().clone())
+        dec.check()
+        for j, g in enumerate(got):
+            i = n_pre - 1 + j
+            rel = ((g - want[i]).norm() / want[i].norm()).item()
+            assert rel <= 2e-2, (n_pre, i, rel)
+    with pytest.raises(ValueError, match="prompt chunk"):
+        dec.prefill(ids[:21])
     # the same steps replayed from the CUDA graph
     dec.capture()
     again = _run(dec, ids)
@@ -101,7 +122,7 @@ def test_position_past_the_cache_is_reported():
     from flashbfp_b200.model import compress_gemma_model
     dev = torch.device("cuda", 0)
     model = compress_gemma_model(_tiny(2).to(dev, torch.bfloat16), OABFCompressor())
-    dec = GemmaDecoder.from_hf(model, max_ctx=8)
+    dec = GemmaDecoder.from_hf(model, max_ctx=8, max_prefill=4)
     dec.reset(8)                                 # one past the last cache row: nothing is written
     dec.step()
     with pytest.raises(RuntimeError, match="position outside the KV cache"):
