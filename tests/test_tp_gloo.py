@@ -17,7 +17,7 @@ import torch.multiprocessing as mp
 
 from oracle import oabf
 
-N, K = 256, 320           # 2 ranks: 128-row shards, 160-column (10-block) shards
+N, K = 256, 320           # 2 ranks: 128-row shards; K in whole 256-column stages: 256 + 64 columns
 
 
 def _free_port():
@@ -109,6 +109,26 @@ def test_split_plans_cover_exactly():
     assert tp.mode_of("q_proj") == "column"
     with pytest.raises(ValueError):
         tp.mode_of("lm_head")
+
+
+def test_row_parallel_shards_are_whole_stages():
+    """Row-parallel shards of the 12B-class linears split K in whole 256-column stages at TP 2, 4
+    and 8 (so every shard takes the tensor-core GEMV and its fused exchange), covering K exactly;
+    the weight slice and the input range agree."""
+    from flashbfp_b200 import tp, workloads
+    for name in ("o_proj", "down_proj"):
+        n, k = workloads.GEMMA12B_LAYER[name]
+        W = torch.zeros(n, k)
+        for world in (2, 4, 8):
+            ranges = [tp.input_range(name, k, r, world) for r in range(world)]
+            assert ranges[0][0] == 0 and ranges[-1][1] == k
+            assert all(a[1] == b[0] for a, b in zip(ranges, ranges[1:]))
+            assert all((hi - lo) % tp.ROW_K_ALIGN == 0 and hi > lo for lo, hi in ranges), (name, world, ranges)
+            sizes = [hi - lo for lo, hi in ranges]
+            assert max(sizes) - min(sizes) <= tp.ROW_K_ALIGN
+            for r, (lo, hi) in enumerate(ranges):
+                assert tp.weight_slice(W, name, r, world).shape == (n, hi - lo)
+    assert tp.input_range("q_proj", 3840, 1, 4) == (0, 3840)
 
 
 def test_tensor_parallel_two_gloo_ranks():
