@@ -10,13 +10,19 @@ to OABF (block 16; weights N(0, 0.02) bf16 with 1.5% StudentT(3)*20*0.02 outlier
 gate|up are fused launches, so one step = one decode token (M activations of bf16) through
 192 fused dequant-GEMV launches reading ~7.4 GB of packed weights (inputs far larger than
 L2, so no flush is needed). Tensor parallelism over N ranks: q/k/v/gate/up split their output
-rows, o/down split their input blocks and all-reduce (NCCL) their fp32 partial outputs.
+rows, o/down split their input in whole 256-column stages and sum their partial outputs across
+ranks, by default inside the GEMV itself (``--exchange fused``: peer-memory push and ordered sum
+over NVLink in the epilogue; ``allreduce``: a separate NVLink all-reduce kernel; ``nccl``).
 
 ``value`` = algorithmic bytes per step over all ranks (11 B per 16-weight block + 10 B per
-outlier + bf16 X and Y) / step time, max over ranks. Kernels are replayed from CUDA graphs
-(one graph per layer kind, 48 launches each) with CUDA events between them. ``e2e`` runs the
-same step through the public ``OABFLinear`` modules with the activations copied from pinned
-host memory each step and the outputs copied back.
+outlier + bf16 X and Y) / step time, max over ranks. The headline step is one CUDA graph of the
+192 launches in model order, timed with CUDA events; per-kind graphs give the per-kind rates and
+the roofline kernel. ``e2e`` runs the same step through the public ``OABFLinear`` modules with
+the activations copied from pinned host memory each step and the outputs copied back. At N = 1
+the line also carries ``model_decode`` (whole tokens of a random-init 12B-class Gemma-3 around
+these linears: embedding, norms, RoPE, KV cache, attention, GeGLU, bf16 lm_head and the greedy
+pick in one CUDA graph per token), ``prefill`` (the gate|up linear at M = 2048 on the tcgen05
+prefill GEMM), ``bf16_cublas_decode`` and ``compress``.
 """
 from __future__ import annotations
 
