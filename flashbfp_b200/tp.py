@@ -1,10 +1,12 @@
-"""Tensor parallelism for OABF linears: one process per GPU, torch.distributed for the exchange.
+"""Tensor parallelism for OABF linears: one process per GPU.
 
 Column-parallel linears (q/k/v/gate/up: they share the layer input and feed per-head or
 element-wise work) keep a slice of output rows on every rank and need no collective.
 Row-parallel linears (o/down: their input is already sharded by the previous column-parallel
-layer) keep a slice of input block-columns and add their fp32 partial outputs with one
-all-reduce. The outlier threshold of the reference is a whole-matrix statistic
+layer) keep a slice of the input in whole 256-column stages, and the ranks' fp32 partial
+outputs are summed: inside the GEMV itself over NVLink peer memory (``NVLinkAllReduce`` handle
+with ``packed_linear_allreduce``), by a separate peer-memory all-reduce kernel, or by the
+process group's all-reduce. The outlier threshold of the reference is a whole-matrix statistic
 (flash_bfp/compressor.py:11-32), so every shard is compressed with the threshold of the whole
 matrix; its bytes then equal the corresponding slice of the whole matrix's compression.
 """
