@@ -6,8 +6,11 @@ constructor, ``load_from_weight``, ``forward`` and the ``state_dict`` key layout
 the reference there is no CPU fallback: inputs must be CUDA tensors and the CUDA library
 must be built, otherwise the call raises.
 
-Device-resident form of a layer (11 bytes per 16 weights + 4 bytes per outlier): the
-reference's packed bytes plus the outliers grouped for the fused kernels (``packed.py``).
+Device-resident form of a layer (``packed.py``): the reference's packed bytes (11 per 16
+weights) plus each outlier twice, in the reference's COO form (10 bytes, kept for state_dict,
+slicing and saving) and grouped for the fused kernels (4 bytes). ``packed_linear`` sends up to
+16 tokens per launch through the decode GEMV and more through the tcgen05 prefill GEMM;
+``packed_linear_allreduce`` is the row-parallel GEMV with the cross-rank sum fused in.
 """
 from __future__ import annotations
 
