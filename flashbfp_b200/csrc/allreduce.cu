@@ -19,7 +19,9 @@
 // Reusing a parity two calls later is safe: a rank starts call e + 2 only after it has received
 // every peer's words of call e + 1, which peers sent after finishing call e (stream order). Every
 // wait is bounded: after about two seconds the kernel records an error (fbfp_allreduce_check)
-// and the CTA returns.
+// and the CTA returns. The buffer layout lives in exchange.cuh: the decode GEMV's fused exchange
+// (fbfp_gemv_allreduce, gemv_tc.cu) uses the same buffers and the same call counter, so both
+// kinds of call may be mixed on one stream, in the same order on every rank.
 #include <cuda_runtime.h>
 #include <stdint.h>
 #include <string.h>
