@@ -335,8 +335,15 @@ extern "C" int64_t fbfp_gemv_workspace_bytes(int64_t m, int64_t npad) {
   return (int64_t)(256 + ws_counters_bytes(npad) + align256(sizeof(float) * (size_t)(m * npad)));
 }
 
+namespace fbfp {
+int noalloc_scratch(void** out);
+}
+
 extern "C" int fbfp_gemv_check(void* workspace, void* stream) {
-  FBFP_CHECK_ARG(workspace, "null workspace");
+  if (!workspace) {                       // the built-in scratch of fbfp_gemv_noalloc
+    const int rc = noalloc_scratch(&workspace);
+    if (rc != FBFP_OK) return rc;
+  }
   cudaStream_t st = as_stream(stream);
   int32_t* errp = reinterpret_cast<int32_t*>(workspace);
   int32_t h = 0;
@@ -359,13 +366,13 @@ int allreduce_buffers(void* handle, uint8_t** bufs, int* world, int* rank, int64
 // the stream, so the tcgen05 kernel may fetch its first weight stages before that kernel ends.
 // allreduce != null: the row-parallel exchange through that all-reduce handle is fused into the
 // tcgen05 kernel's epilogue (y = bias + the sum over ranks of their partial products).
-static int gemv_impl(const void* x, int x_dtype, int64_t m, int64_t ldx,
-                     const int8_t* exponents, const int16_t* signs, const int32_t* payload,
-                     int64_t n_out, int64_t k_in, int64_t kpad, int64_t npad,
-                     const uint32_t* entries, const int32_t* seg_ptr, const void* bias,
-                     int bias_dtype, void* y, int y_dtype, int64_t ldy, void* workspace,
-                     void* stream, int resident, void* allreduce) {
-  FBFP_CHECK_ARG(x && exponents && signs && payload && y && workspace, "null pointer");
+namespace fbfp {
+// Argument checks shared by every GEMV entry point (the workspace is checked by the caller).
+int gemv_validate(const void* x, int x_dtype, int64_t m, int64_t ldx, const int8_t* exponents,
+                  const int16_t* signs, const int32_t* payload, int64_t n_out, int64_t k_in,
+                  int64_t kpad, int64_t npad, const uint32_t* entries, const int32_t* seg_ptr,
+                  const void* bias, int bias_dtype, const void* y, int y_dtype, int64_t ldy) {
+  FBFP_CHECK_ARG(x && exponents && signs && payload && y, "null pointer");
   FBFP_CHECK_ARG(m >= 1 && m <= 16, "fbfp_gemv needs 1 <= m <= 16 (got %lld)", (long long)m);
   FBFP_CHECK_ARG(dtype_ok(x_dtype), "x_dtype must be f32, bf16 or f16");
   FBFP_CHECK_ARG(dtype_ok(y_dtype), "y_dtype must be f32, bf16 or f16");
@@ -375,6 +382,20 @@ static int gemv_impl(const void* x, int x_dtype, int64_t m, int64_t ldx,
   FBFP_CHECK_ARG(ldx >= k_in && ldy >= n_out, "bad leading dimension");
   FBFP_CHECK_ARG(!entries || seg_ptr, "entries without seg_ptr");
   FBFP_CHECK_ARG(((uintptr_t)payload & 7) == 0, "payload must be 8-byte aligned");
+  return FBFP_OK;
+}
+}  // namespace fbfp
+
+static int gemv_impl(const void* x, int x_dtype, int64_t m, int64_t ldx,
+                     const int8_t* exponents, const int16_t* signs, const int32_t* payload,
+                     int64_t n_out, int64_t k_in, int64_t kpad, int64_t npad,
+                     const uint32_t* entries, const int32_t* seg_ptr, const void* bias,
+                     int bias_dtype, void* y, int y_dtype, int64_t ldy, void* workspace,
+                     void* stream, int resident, void* allreduce) {
+  const int vrc = gemv_validate(x, x_dtype, m, ldx, exponents, signs, payload, n_out, k_in, kpad, npad,
+                                entries, seg_ptr, bias, bias_dtype, y, y_dtype, ldy);
+  if (vrc != FBFP_OK) return vrc;
+  FBFP_CHECK_ARG(workspace, "null pointer (workspace)");
   FBFP_CHECK_ARG(((uintptr_t)workspace & 255) == 0, "workspace must be 256-byte aligned");
   const int64_t kb_row = kpad / kBlock;
   const int n_chunks = (int)((kb_row + kChunkKb - 1) / kChunkKb);

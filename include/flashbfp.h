@@ -99,7 +99,8 @@ int fbfp_outlier_tiles_build(const int32_t* block_idx, const int32_t* offset, co
  * ---------------------------------------------------------------------------------- */
 int64_t fbfp_gemv_workspace_bytes(int64_t m, int64_t npad);
 /* Synchronises `stream` and reports FBFP_ERR_TIMEOUT if a kernel that used `workspace`
- * gave up a bounded device-side wait since the last check (then clears the record). */
+ * gave up a bounded device-side wait since the last check (then clears the record).
+ * workspace NULL: the built-in scratch of fbfp_gemv_noalloc on the current device. */
 int fbfp_gemv_check(void* workspace, void* stream);
 int fbfp_gemv(const void* x, int x_dtype, int64_t m, int64_t ldx,
               const int8_t* exponents, const int16_t* signs, const int32_t* payload,
@@ -195,8 +196,11 @@ int fbfp_allreduce_destroy(void* handle);
  * Same arguments and results as fbfp_gemv, minus `workspace`: the scratch lives in an 8 MiB
  * array compiled into the library (every GPU that loads the library holds it until exit).
  * Returns FBFP_ERR_ARG when fbfp_gemv_workspace_bytes(m, npad) exceeds 8 MiB (about 130,000
- * padded rows at m = 16). Allocates nothing; each call clears the part of the array it uses.
- * The first call on a device looks up the array's device address (cudaGetSymbolAddress):
+ * padded rows at m = 16); every argument is checked before anything is enqueued. Allocates
+ * nothing; each call clears the part of the array it uses except its error word: a bounded
+ * device-side wait that gave up stays recorded there until fbfp_gemv_check(NULL, stream)
+ * reports it (FBFP_ERR_TIMEOUT) and clears it. The first call on a device (and the first after
+ * the device's context changes) looks up the array's device address (cudaGetSymbolAddress):
  * make that first call outside any stream capture. All calls on a device share the one
  * array, so calls that overlap on the GPU (other streams, other host threads) race and
  * corrupt each other's results: serialise them. */

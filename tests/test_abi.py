@@ -36,6 +36,11 @@ def test_argument_errors_without_gpu(L):
     assert b"null" in L.fbfp_last_error()
     st = L.fbfp_dequant(None, None, None, 1, 1, 16, 0, None, 1, None)
     assert st == 1
+    # the no-allocation entry checks its arguments before it touches the device or the stream
+    st = L.fbfp_gemv_noalloc(None, 1, 1, 16, None, None, None, 16, 16, 16, 64, None, None, None, 0,
+                             None, 1, 16, None)
+    assert st == 1
+    assert b"null" in L.fbfp_last_error()
     with pytest.raises(ValueError):
         _lib.check(1, "probe")
     with pytest.raises(NotImplementedError):
