@@ -45,6 +45,11 @@ _PROTOS = {
                                      _c_i64, _vp, _vp, _vp, _c_int, _vp, _c_int, _c_i64, _vp, _vp, _c_int,
                                      _vp]),
     "fbfp_stream_fence": (_c_int, [_vp]),
+    "fbfp_records_bytes": (_c_i64, [_c_i64, _c_i64, _c_i64]),
+    "fbfp_records_scratch_bytes": (_c_i64, [_c_i64, _c_i64]),
+    "fbfp_records_build": (_c_int, [_vp, _vp, _vp, _c_i64, _c_i64, _vp, _vp, _c_i64, _vp, _vp, _vp, _vp]),
+    "fbfp_gemv_records": (_c_int, [_vp, _c_i64, _c_i64, _vp, _c_i64, _c_i64, _c_i64, _c_i64,
+                                   _vp, _c_int, _vp, _c_int, _c_i64, _vp, _vp, _c_int, _vp]),
     "fbfp_embed": (_c_int, [_vp, _c_i64, _vp, _c_i64, _c_i64, ctypes.c_float, _vp, _vp, _vp]),
     "fbfp_rmsnorm": (_c_int, [_vp, _c_i64, _vp, ctypes.c_float, _c_i64, _vp, _vp]),
     "fbfp_post_residual_norm": (_c_int, [_vp, _c_i64, _vp, _vp, _vp, ctypes.c_float, _c_i64, _vp, _vp]),
@@ -58,6 +63,7 @@ _PROTOS = {
     "fbfp_allreduce_create": (_c_int, [_c_int, _c_int, _c_i64, _vp, _vp]),
     "fbfp_allreduce_open_peer": (_c_int, [_vp, _c_int, _vp]),
     "fbfp_allreduce_sum_f32": (_c_int, [_vp, _vp, _c_i64, _vp]),
+    "fbfp_allreduce_set_timeout": (_c_int, [_vp, _c_i64]),
     "fbfp_allreduce_check": (_c_int, [_vp, _vp]),
     "fbfp_allreduce_destroy": (_c_int, [_vp]),
     "fbfp_gemm_prefill": (_c_int, [_vp, _c_int, _c_i64, _c_i64, _vp, _vp, _vp, _c_i64, _c_i64, _c_i64,

@@ -18,8 +18,8 @@
 //   3. epoch = tag.
 // Reusing a parity two calls later is safe: a rank starts call e + 2 only after it has received
 // every peer's words of call e + 1, which peers sent after finishing call e (stream order). Every
-// wait is bounded: after about two seconds the kernel records an error (fbfp_allreduce_check)
-// and the CTA returns. The buffer layout lives in exchange.cuh: the decode GEMV's fused exchange
+// wait is bounded (two seconds by default, fbfp_allreduce_set_timeout): then the kernel records an
+// error (fbfp_allreduce_check) and the CTA returns. The buffer layout lives in exchange.cuh: the decode GEMV's fused exchange
 // (fbfp_gemv_allreduce, gemv_tc.cu) uses the same buffers and the same call counter, so both
 // kinds of call may be mixed on one stream, in the same order on every rank.
 #include <cuda_runtime.h>
@@ -38,6 +38,7 @@ constexpr size_t kArHeader = kXHeader;
 struct ArHandle {
   int world = 0, rank = 0, device = 0;
   int64_t max_elems = 0;
+  uint64_t timeout_ns = 2000000000ull;      // bound of every wait on a peer's words
   uint8_t* base = nullptr;                  // this rank's buffer
   uint8_t* peer[kMaxWorld] = {nullptr};     // every rank's buffer (self included)
   bool opened[kMaxWorld] = {false};
@@ -46,6 +47,7 @@ struct ArHandle {
 struct ArArgs {
   float* y;
   int64_t n;
+  uint64_t timeout_ns;
   int world, rank;
   int64_t max_elems;
   uint8_t* peer[kMaxWorld];
@@ -74,23 +76,30 @@ __global__ void __launch_bounds__(kArThreads, 1) allreduce_sum_kernel(const ArAr
     uint2* dst = ar_slot(a.peer[p], a.max_elems, par, a.rank);
     for (int64_t i = tid; i < a.n; i += kArThreads) st_word(dst + i, __float_as_uint(a.y[i]), tag);
   }
-  // 2. receive and sum in rank order (each thread its own elements); a wait that gives up sets
-  // s_fail, and every thread then skips to the barrier
+  // 2. receive and sum in rank order (each thread its own elements); a wait that gives up (after
+  // a.timeout_ns of the global timer) sets s_fail, and every thread then skips to the barrier
   bool stop = false;
   for (int64_t i = tid; i < a.n && !stop; i += kArThreads) {
     float acc = 0.f;
     for (int q = 0; q < a.world && !stop; ++q) {
       const uint2* src = ar_slot(a.self, a.max_elems, par, q) + i;
       uint2 w = ld_word(src);
-      for (uint32_t it = 0; w.y != tag; ++it) {
-        if (it >= (1u << 25) || s_fail) {
-          if (!s_fail) { s_fail = 1; atomicExch(ar_err(a.self), 1 + q); }
-          stop = true;
-          break;
+      uint64_t t0 = 0;
+      for (uint32_t it = 1; w.y != tag; ++it) {
+        if ((it & 63) == 0) {
+          uint64_t now;
+          asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(now));
+          if (t0 == 0) t0 = now;
+          if (s_fail || now - t0 > a.timeout_ns) {
+            if (!s_fail) { s_fail = 1; atomicExch(ar_err(a.self), 1 + q); }
+            stop = true;
+            break;
+          }
         }
         if (it > 256) __nanosleep(64);
         w = ld_word(src);
       }
+      if (stop) break;
       acc += __uint_as_float(w.x);
     }
     if (!stop) a.y[i] = acc;
@@ -139,6 +148,9 @@ extern "C" int fbfp_allreduce_create(int world, int rank, int64_t max_elems, voi
 extern "C" int64_t fbfp_allreduce_ipc_handle_bytes() { return (int64_t)sizeof(cudaIpcMemHandle_t); }
 
 namespace fbfp {
+uint64_t allreduce_timeout_ns(void* handle) {
+  return reinterpret_cast<ArHandle*>(handle)->timeout_ns;
+}
 // For the GEMV's fused exchange: the ranks' buffers of a handle whose peers are all open.
 int allreduce_buffers(void* handle, uint8_t** bufs, int* world, int* rank, int64_t* max_elems) {
   ArHandle* h = reinterpret_cast<ArHandle*>(handle);
@@ -176,7 +188,8 @@ extern "C" int fbfp_allreduce_sum_f32(void* handle, float* y, int64_t n, void* s
     FBFP_CHECK_ARG(h->opened[p], "peer %d has not been opened", p);
   if (n == 0) return FBFP_OK;
   ArArgs a;
-  a.y = y; a.n = n; a.world = h->world; a.rank = h->rank; a.max_elems = h->max_elems;
+  a.y = y; a.n = n; a.timeout_ns = h->timeout_ns;
+  a.world = h->world; a.rank = h->rank; a.max_elems = h->max_elems;
   for (int p = 0; p < kMaxWorld; ++p) a.peer[p] = p < h->world ? h->peer[p] : nullptr;
   a.self = h->base;
   // programmatic stream serialisation: the launch overlaps the previous kernel's drain; the
@@ -193,6 +206,15 @@ extern "C" int fbfp_allreduce_sum_f32(void* handle, float* y, int64_t n, void* s
   cfg.numAttrs = 1;
   FBFP_CUDA_TRY(cudaLaunchKernelEx(&cfg, allreduce_sum_kernel, a));
   FBFP_LAUNCH_CHECK("allreduce_sum_kernel");
+  return FBFP_OK;
+}
+
+extern "C" int fbfp_allreduce_set_timeout(void* handle, int64_t timeout_us) {
+  ArHandle* h = reinterpret_cast<ArHandle*>(handle);
+  FBFP_CHECK_ARG(h, "null pointer");
+  FBFP_CHECK_ARG(timeout_us >= 1 && timeout_us <= 60000000, "timeout %lld us outside [1 us, 60 s]",
+                 (long long)timeout_us);
+  h->timeout_ns = (uint64_t)timeout_us * 1000ull;
   return FBFP_OK;
 }
 

@@ -336,6 +336,18 @@ extern "C" int64_t fbfp_gemv_workspace_bytes(int64_t m, int64_t npad) {
 }
 
 namespace fbfp {
+// The regions of a GEMV workspace for a matrix of npad rows (shared with gemv_rec.cu).
+int gemv_workspace_parts(void* workspace, int64_t npad, int32_t** err, int32_t** counters, float** ws) {
+  FBFP_CHECK_ARG(workspace, "null workspace");
+  char* base = reinterpret_cast<char*>(workspace);
+  *err = reinterpret_cast<int32_t*>(base);
+  *counters = reinterpret_cast<int32_t*>(base + 256);
+  *ws = reinterpret_cast<float*>(base + 256 + ws_counters_bytes(npad));
+  return FBFP_OK;
+}
+}  // namespace fbfp
+
+namespace fbfp {
 int noalloc_scratch(void** out);
 }
 
@@ -360,6 +372,7 @@ extern "C" int fbfp_gemv_check(void* workspace, void* stream) {
 
 namespace fbfp {
 int allreduce_buffers(void* handle, uint8_t** bufs, int* world, int* rank, int64_t* max_elems);
+uint64_t allreduce_timeout_ns(void* handle);
 }
 
 // resident != 0: the packed weights and outlier index were not written by the previous kernel in
@@ -430,13 +443,14 @@ static int gemv_impl(const void* x, int x_dtype, int64_t m, int64_t ldx,
     t.n_stages = (int)(kb_row / kStageKb);
     t.total_units = ((npad + kGroupRows - 1) / kGroupRows) * t.n_stages;
     t.early_weights = resident ? 1 : 0;
-    t.world = 1; t.rank = 0; t.xmax = 0; t.exit_count = errp + 1;
+    t.world = 1; t.rank = 0; t.xmax = 0; t.exit_count = errp + 1; t.xchg_timeout_ns = 0;
     for (int p = 0; p < 8; ++p) t.xbuf[p] = nullptr;
     if (allreduce) {
       int rc = allreduce_buffers(allreduce, t.xbuf, &t.world, &t.rank, &t.xmax);
       if (rc != FBFP_OK) return rc;
       FBFP_CHECK_ARG(m * n_out <= t.xmax, "m * n_out = %lld exceeds the all-reduce handle's %lld elements",
                      (long long)(m * n_out), (long long)t.xmax);
+      t.xchg_timeout_ns = allreduce_timeout_ns(allreduce);
     }
     return launch_gemv_tc(t, st);
   }

@@ -411,7 +411,7 @@ __device__ __forceinline__ uint64_t global_ns() {
   return t;
 }
 
-// Waits (bounded: about four seconds, or until another role of the CTA aborts) for the word of
+// Waits (bounded by the all-reduce handle's timeout, or until another role of the CTA aborts) for the word of
 // this call's tag at `src` and returns its value in *v.
 __device__ __forceinline__ bool tc_xchg_wait(const TcShared& S, const TcArgs& a, const uint2* src,
                                              uint32_t tag, int code, float* v) {
@@ -423,7 +423,7 @@ __device__ __forceinline__ bool tc_xchg_wait(const TcShared& S, const TcArgs& a,
       const uint64_t now = global_ns();
       if (t0 == 0) {
         t0 = now;
-      } else if (now - t0 > 4000000000ull) {
+      } else if (now - t0 > a.xchg_timeout_ns) {
         *S.abort_flag = 1;
         atomicExch(a.err, code);
         return false;

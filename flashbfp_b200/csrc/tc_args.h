@@ -30,5 +30,6 @@ struct TcArgs {
   uint8_t* xbuf[8];
   int64_t xmax;          // elements per (parity, source) slot
   int32_t* exit_count;   // CTAs of this call that have finished (in the workspace, zero between calls)
+  uint64_t xchg_timeout_ns;  // bound of every wait on a peer's words (the all-reduce handle's)
 };
 }  // namespace fbfp

@@ -49,6 +49,32 @@ def check_device_errors(device=None) -> None:
             _lib.check(L.fbfp_gemv_check(_lib.ptr(ws), _lib.ctypes.c_void_p(sptr)), "fbfp_gemv_check")
 
 
+GEMV_RESIDENT, GEMV_DENSE_ONLY, GEMV_TENSOR_CORES = 1, 4, 8
+
+
+def records_eligible(X: torch.Tensor, pw: PackedWeight) -> bool:
+    """Whether the stage-record GEMV takes X (at most 16 tokens per launch) on pw."""
+    return (pw.records is not None and X.dtype == torch.bfloat16 and X.stride(1) == 1
+            and X.stride(0) % 8 == 0 and X.data_ptr() % 16 == 0 and pw.k_in % 8 == 0)
+
+
+def gemv_records(X: torch.Tensor, pw: PackedWeight, Y: torch.Tensor, ws: torch.Tensor,
+                 bias: torch.Tensor | None = None, with_outliers: bool = True, reducer=None,
+                 tensor_cores: bool = False) -> None:
+    """Y[:M] = X[:M] @ W^T (+ outliers) (+ bias) for M <= 16 through fbfp_gemv_records; with
+    ``reducer`` (an NVLinkAllReduce) the row-parallel sum over its ranks is fused in. One token
+    runs on the CUDA cores unless ``tensor_cores``."""
+    L = _lib.lib()
+    bd = _lib.dtype_code(bias.dtype, "bias") if bias is not None else 0
+    flags = ((GEMV_RESIDENT if pw.resident else 0) | (0 if with_outliers else GEMV_DENSE_ONLY)
+             | (GEMV_TENSOR_CORES if tensor_cores else 0))
+    _lib.check(L.fbfp_gemv_records(_lib.ptr(X), X.shape[0], X.stride(0), _lib.ptr(pw.records), pw.n_out,
+                                   pw.k_in, pw.kpad, pw.npad, _lib.ptr(bias), bd, _lib.ptr(Y),
+                                   _lib.dtype_code(Y.dtype, "Y"), Y.stride(0), _lib.ptr(ws),
+                                   reducer.handle if reducer is not None else None, flags,
+                                   _lib.stream_ptr(X.device)), "fbfp_gemv_records")
+
+
 def prefill_eligible(X: torch.Tensor, pw: PackedWeight) -> bool:
     """Shapes the tcgen05 prefill GEMM takes; others run as 16-token GEMV launches."""
     def a16(t):
@@ -88,6 +114,11 @@ def packed_linear(X: torch.Tensor, pw: PackedWeight, bias: torch.Tensor | None =
                                        pw.kpad, pw.npad, _lib.ptr(entries), _lib.ptr(seg_ptr),
                                        _lib.ptr(bias), bd, _lib.ptr(Y), yd, Y.stride(0), _lib.ptr(ws), st),
                    "fbfp_gemm_prefill")
+        return Y
+    if records_eligible(X, pw):
+        for m0 in range(0, M, 16):
+            m = min(16, M - m0)
+            gemv_records(X[m0:m0 + m], pw, Y[m0:m0 + m], ws, bias, with_outliers)
         return Y
     gemv = L.fbfp_gemv_resident if pw.resident else L.fbfp_gemv
     for m0 in range(0, M, 16):
@@ -136,6 +167,11 @@ def packed_linear_allreduce(X: torch.Tensor, pw: PackedWeight, reducer, bias: to
     yd = _lib.dtype_code(out_dtype, "Y")
     ws = gemv_workspace(X.device, pw.npad)
     st = _lib.stream_ptr(X.device)
+    if records_eligible(X, pw):
+        for m0 in range(0, M, 16):
+            m = min(16, M - m0)
+            gemv_records(X[m0:m0 + m], pw, Y[m0:m0 + m], ws, bias, True, reducer)
+        return Y
     for m0 in range(0, M, 16):
         m = min(16, M - m0)
         _lib.check(L.fbfp_gemv_allreduce(_lib.ptr(X[m0:m0 + m]), xd, m, X.stride(0), _lib.ptr(pw.exps),

@@ -3,7 +3,9 @@
 A ``PackedWeight`` holds the reference's packed arrays on the device — exponents
 int8[npad*kb], signs int16[npad*kb], payload int32[npad*kb, 2], block b = n*kb + j — plus
 the outlier list in COO form (block index, offset, fp16 bits; ascending flat order) and in
-the (128-row group, 256-column stage) form the fused kernels read.
+the (128-row group, 256-column stage) form the fused kernels read, and, on request
+(``build_records``), the stage records of ``fbfp_gemv_records`` (one contiguous record per
+128-row group and 256-column stage with its weights, 11 bytes per 16, and its outliers).
 
 Row concatenation serves fused launches (q|k|v, gate|up share their input); row and
 block-column slices serve tensor parallelism. Because the outlier threshold is a
@@ -26,6 +28,7 @@ class PackedWeight:
         self.n_out, self.k_in, self.kpad, self.npad = int(n_out), int(k_in), int(kpad), int(npad)
         self.coo = coo                  # (block_idx int32, offset int32, value bits int16)
         self.entries, self.seg_ptr = entries, seg_ptr
+        self.records = None             # stage records of fbfp_gemv_records (build_records)
         # True once a fence kernel follows the last kernel that wrote these arrays on the current
         # stream: GEMVs may then use fbfp_gemv_resident (weight fetch overlapping the previous
         # kernel's tail)
@@ -54,10 +57,13 @@ class PackedWeight:
             self.coo = tuple(fn(t) for t in self.coo)
         if self.entries is not None:
             self.entries, self.seg_ptr = fn(self.entries), fn(self.seg_ptr)
+        if self.records is not None:
+            self.records = fn(self.records)
         return self
 
     def build_tiles(self) -> "PackedWeight":
-        """(Re)build the tile-grouped outlier entries from the COO list."""
+        """(Re)build the tile-grouped outlier entries from the COO list (and drop stage records
+        built from the previous ones)."""
         L = _lib.lib()
         dev = self.device
         count = self.nnz
@@ -73,9 +79,37 @@ class PackedWeight:
                                                   _lib.ptr(entries), _lib.ptr(seg_ptr),
                                                   _lib.ptr(scratch), _lib.stream_ptr(dev)),
                        "fbfp_outlier_tiles_build")
+            self.entries, self.seg_ptr, self.records = entries, seg_ptr, None
             _lib.check(L.fbfp_stream_fence(_lib.stream_ptr(dev)), "fbfp_stream_fence")
-        self.entries, self.seg_ptr = entries, seg_ptr
         self.resident = True
+        return self
+
+    def build_records(self) -> "PackedWeight":
+        """Build the stage records ``fbfp_gemv_records`` reads (kpad a multiple of 256; about the
+        packed size again in HBM). Raises ValueError for exponents above 120, which the
+        compressor never emits."""
+        L = _lib.lib()
+        if self.entries is None:
+            self.build_tiles()
+        count = self.nnz
+        nbytes = L.fbfp_records_bytes(self.npad, self.kpad, count)
+        if nbytes < 0 or self.payload.data_ptr() % 8 != 0:
+            raise ValueError(f"no stage records for kpad={self.kpad} (a multiple of 256 is needed)")
+        dev = self.device
+        records = torch.empty(nbytes, dtype=torch.uint8, device=dev)
+        scratch = torch.empty(L.fbfp_records_scratch_bytes(self.npad, self.kpad), dtype=torch.uint8, device=dev)
+        bad = torch.zeros(1, dtype=torch.int32, device=dev)
+        with torch.cuda.device(dev):
+            _lib.check(L.fbfp_records_build(_lib.ptr(self.exps), _lib.ptr(self.signs), _lib.ptr(self.payload),
+                                            self.npad, self.kpad, _lib.ptr(self.entries if count else None),
+                                            _lib.ptr(self.seg_ptr if count else None), count,
+                                            _lib.ptr(records), _lib.ptr(bad), _lib.ptr(scratch),
+                                            _lib.stream_ptr(dev)), "fbfp_records_build")
+            if int(bad.item()):
+                raise ValueError(f"{int(bad.item())} blocks have exponents above 120, which the "
+                                 "compressor never emits (dense values are at most 0.2)")
+            self.records = records
+            _lib.check(L.fbfp_stream_fence(_lib.stream_ptr(dev)), "fbfp_stream_fence")
         return self
 
 

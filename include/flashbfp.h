@@ -133,8 +133,9 @@ int fbfp_gemv_resident(const void* x, int x_dtype, int64_t m, int64_t ldx,
  * row-parallel (o, down) shards, packed GEMV + dist.all_reduce of the partial outputs + bias.
  * Requires the tensor-core GEMV (x bf16, 16-byte aligned operands, kpad a multiple of 256, k_in
  * and ldx multiples of 8) and m * n_out <= the handle's max_elems. resident: as
- * fbfp_gemv_resident. A wait that gave up (a peer that never arrives: about four seconds) is
- * reported by fbfp_gemv_check on the workspace; the handle is unusable after that. The handle's
+ * fbfp_gemv_resident. A wait that gave up (a peer that never arrives within the handle's timeout,
+ * fbfp_allreduce_set_timeout) is reported by fbfp_gemv_check on the workspace; the handle is
+ * unusable after that. The handle's
  * call counter is shared with fbfp_allreduce_sum_f32, so both may be mixed on one stream, in the
  * same order on every rank. No counterpart in the reference (single-GPU only). */
 int fbfp_gemv_allreduce(const void* x, int x_dtype, int64_t m, int64_t ldx,
@@ -144,6 +145,50 @@ int fbfp_gemv_allreduce(const void* x, int x_dtype, int64_t m, int64_t ldx,
                         const void* bias, int bias_dtype,
                         void* y, int y_dtype, int64_t ldy,
                         void* workspace, void* allreduce, int resident, void* stream);
+/* ------------------------------------------------------------------------------------
+ * Stage records: the decode GEMV's own device layout of a packed matrix and its outliers, built
+ * once at load time from the reference arrays and the outlier layout above (kpad a multiple of
+ * 256). A table of int64 byte offsets (one per record plus the end, padded to 256 bytes), then
+ * one record per (128-row group g, 256-column stage st), index g * (kpad / 256) + st: every
+ * weight as the 5-bit value 16 + s*m (80 bits per 16-weight block, as the reference's signs +
+ * nibbles), each block's exponent biased by 134, then the record's outliers (136 uint16 row
+ * starts and the uint32 entries of fbfp_outlier_tiles_build). So 11 bytes per 16 weights plus
+ * 4 per outlier, and one bulk copy brings a record's weights and outliers together.
+ * fbfp_records_bytes(npad, kpad, outliers) is the size to allocate (outliers = the COO count; an
+ * upper bound on what the build writes) and fbfp_records_scratch_bytes the scratch the build
+ * needs; both return -1 unless kpad is a multiple of 256. `records` must be 256-byte aligned.
+ * Exponents above 120 (the compressor emits at most -3) cannot be biased into a byte:
+ * `bad_exponents` (optional device int32, caller zeroes it) counts such blocks. Replaces the
+ * GPU-side widening of the packed arrays and the outlier cache of OABFLinear.load_from_weight
+ * (flash_bfp/triton_kernel.py:232-291).
+ * ---------------------------------------------------------------------------------- */
+int64_t fbfp_records_bytes(int64_t npad, int64_t kpad, int64_t outliers);
+int64_t fbfp_records_scratch_bytes(int64_t npad, int64_t kpad);
+int fbfp_records_build(const int8_t* exponents, const int16_t* signs, const int32_t* payload,
+                       int64_t npad, int64_t kpad, const uint32_t* entries, const int32_t* seg_ptr,
+                       int64_t outliers, void* records, int32_t* bad_exponents, void* scratch,
+                       void* stream);
+
+/* Decode GEMV on stage records: the same product as fbfp_gemv (y = x W_full^T + bias, fp32
+ * accumulate, the records' outliers included) for bf16 x (16-byte aligned, ldx and k_in
+ * multiples of 8) and 1 <= m <= 16. Replaces oabf_gemm (triton_kernel.py:130-195, the
+ * oabf_gemm_kernel tiles of :22-86) and the outlier SpMV (:339-356) and bias add (:358-362) of
+ * OABFLinear.forward. `workspace` as for fbfp_gemv.
+ * allreduce: NULL, or an all-reduce handle whose peers are all open to fuse the row-parallel
+ * exchange into the kernel as fbfp_gemv_allreduce does (y = bias + sum over ranks, in rank
+ * order, of the ranks' partial products; same bits on every rank).
+ * flags: FBFP_GEMV_RESIDENT as fbfp_gemv_resident (the records were not written by the kernel
+ * just before this call in `stream`, so the first records are fetched while that kernel
+ * finishes); FBFP_GEMV_DENSE_ONLY leaves the outliers out (the dense part, as oabf_gemm).
+ * One token (m = 1) runs on the CUDA cores (fp32 FMAs), more on the tensor cores (tcgen05, one
+ * M=128 x N=16 x K=16 MMA per 16-weight block column); FBFP_GEMV_TENSOR_CORES sends one token to
+ * the tensor cores too. */
+enum { FBFP_GEMV_RESIDENT = 1, FBFP_GEMV_DENSE_ONLY = 4, FBFP_GEMV_TENSOR_CORES = 8 };
+int fbfp_gemv_records(const void* x, int64_t m, int64_t ldx, const void* records,
+                      int64_t n_out, int64_t k_in, int64_t kpad, int64_t npad,
+                      const void* bias, int bias_dtype, void* y, int y_dtype, int64_t ldy,
+                      void* workspace, void* allreduce, int flags, void* stream);
+
 /* Launches an empty kernel on `stream`: placed after the kernels that write a matrix's packed
  * arrays, it makes the matrix resident for fbfp_gemv_resident. No counterpart in the reference. */
 int fbfp_stream_fence(void* stream);
@@ -178,14 +223,16 @@ int fbfp_gemm_prefill(const void* x, int x_dtype, int64_t m, int64_t ldx,
  * the handles between ranks (any host channel) and call fbfp_allreduce_open_peer for every
  * other rank. fbfp_allreduce_sum_f32 then replaces y[0..n) (n <= max_elems) on every rank with
  * the sum over ranks, in rank order (bit-identical on every rank); all ranks must make the same
- * calls in the same order. A wait that gives up (about two seconds: a rank that never
- * arrives) is reported by fbfp_allreduce_check as FBFP_ERR_TIMEOUT. Graph-capturable.
+ * calls in the same order. A wait that gives up (a rank that never arrives within the handle's
+ * timeout: two seconds unless fbfp_allreduce_set_timeout changed it, between 1 us and 60 s) is
+ * reported by fbfp_allreduce_check as FBFP_ERR_TIMEOUT. Graph-capturable.
  * ---------------------------------------------------------------------------------- */
 int64_t fbfp_allreduce_ipc_handle_bytes(void);
 int fbfp_allreduce_create(int world, int rank, int64_t max_elems, void** handle,
                           void* ipc_handle_out);
 int fbfp_allreduce_open_peer(void* handle, int peer, const void* ipc_handle);
 int fbfp_allreduce_sum_f32(void* handle, float* y, int64_t n, void* stream);
+int fbfp_allreduce_set_timeout(void* handle, int64_t timeout_us);
 int fbfp_allreduce_check(void* handle, void* stream);
 int fbfp_allreduce_destroy(void* handle);
 
