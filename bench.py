@@ -699,92 +699,102 @@ def _traffic(m):
 
 
 # --------------------------------------------------------------------------------------
-# CPU baseline (the oracle port of the reference's CPU path) and the reference arm
+# CPU baseline and reference arm: the torch restatement of the reference's CPU path
+# (oracle/cpu_torch.py; same torch operations and dtypes, bit-identical outputs, cost within a
+# few percent of the reference's own code where both were timed: oracle/port_calibration.json)
 # --------------------------------------------------------------------------------------
-def _cpu_layer(n, k, seed, rows=None):
-    from flashbfp_b200 import workloads
-    from oracle import oabf
-    W = workloads.decode_weight(n, k, seed=seed)
-    if rows is not None:
-        W = W[:rows]
-    dp, sp = oabf.compress_matrix(W.float().numpy(), "bf16")
-    r, c, v = oabf.outlier_rcv(sp, dp["padded_shape"], W.shape[1], W.shape[0])
-    return dp, sp, (r, c, v)
-
-
-def _cpu_threads():
+def _calibration():
     try:
-        from threadpoolctl import threadpool_info
-        return max([i.get("num_threads", 1) for i in threadpool_info()] or [1])
+        with open(os.path.join(os.path.dirname(os.path.abspath(__file__)), "oracle",
+                               "port_calibration.json")) as f:
+            c = json.load(f)
+        run = max(c["runs"], key=lambda r: r["threads"])
+        return {"forward": run["forward"]["reference_over_port"],
+                "compress": run["compress"]["reference_over_port"],
+                "measured": f"reference / port time on {c['shape'][0]}x{c['shape'][1]} bf16, "
+                            f"{run['threads']} threads, {c['cpus']}-CPU host"}
     except Exception:
-        return 1
+        return None
 
 
-def cpu_baseline_sample(seconds):
-    """Time the port of the reference CPU forward (unpack + matmul + outliers) on o_proj."""
-    import numpy as np
-    from oracle.cpu_baseline import fallback_forward
-    n, k = 3840, 4096
-    dp, sp, (r, c, v) = _cpu_layer(n, k, seed=4242)
-    X = np.random.default_rng(0).standard_normal((1, k)).astype(np.float32)
-    nbytes = 11 * dp["exponents"].size + 10 * sp["count"] + 2 * k + 2 * n
-    fallback_forward(X, dp["exponents"], dp["signs"], dp["payload"], dp["padded_shape"], dp["orig_shape"], r, c, v)
+def _timed(fn, seconds, max_iters=1000):
+    fn()
     t0 = time.perf_counter()
     it = 0
     while True:
-        fallback_forward(X, dp["exponents"], dp["signs"], dp["payload"], dp["padded_shape"],
-                         dp["orig_shape"], r, c, v)
+        fn()
         it += 1
         el = time.perf_counter() - t0
-        if (el >= seconds and it >= 3) or it >= 1000:
-            break
-    return {"value": round(nbytes * it / el / 1e9, 4), "unit": "GB/s", "cores": _cpu_threads(),
+        if (el >= seconds and it >= 3) or it >= max_iters:
+            return it, el
+
+
+def cpu_baseline_sample(seconds):
+    """The reference's CPU forward (unpack + matmul + outliers) on the full o_proj at M=1 and
+    its compressor on the same matrix, on all host threads torch uses."""
+    import torch
+    from flashbfp_b200 import workloads
+    from oracle import cpu_torch
+    n, k = 3840, 4096
+    W = workloads.decode_weight(n, k, seed=4242)
+    X = workloads.activations(1, k, seed=0)
+    dp, sp = cpu_torch.compress_matrix(W)
+    rcv = cpu_torch.outlier_rcv(sp, dp["padded_shape"], n, k)
+    fb = cpu_torch.algorithmic_bytes_forward(dp, sp["count"], 1, 2)
+    it, el = _timed(lambda: cpu_torch.fallback_forward(X, dp, rcv), seconds / 2)
+    cb = cpu_torch.algorithmic_bytes_compress(W, dp, sp["count"])
+    itc, elc = _timed(lambda: cpu_torch.compress_matrix(W), seconds / 2)
+    return {"value": round(fb * it / el / 1e9, 4), "unit": "GB/s", "cores": cpu_torch.threads(),
             "kind": "port", "host_cpus": os.cpu_count(),
-            "sample": f"o_proj 3840x4096 OABF at M=1, {it} forwards in {el:.1f} s (numpy port of "
-                      "_cpu_fallback_gemm + outlier index_add; unpack single-threaded, matmul on BLAS threads)"}
+            "sample": f"o_proj 3840x4096 bf16 OABF at M=1: {it} CPU forwards in {el:.1f} s "
+                      "(torch restatement of _cpu_fallback_gemm + outlier index_add_)",
+            "compress_gbs": round(cb * itc / elc / 1e9, 4),
+            "compress_sample": f"compress_matrix of the same bf16 matrix: {itc} runs in {elc:.1f} s",
+            "reference_over_port": _calibration()}
 
 
 def run_reference(args):
-    """Reference arm: the CPU port on the host cores, same metric, bounded per-step sample."""
-    import numpy as np
-    from oracle.cpu_baseline import fallback_forward
+    """Reference arm: the reference's CPU path (torch restatement) on the host cores, same metric;
+    one step = the four linears of one 12B-class decoder layer at full size, M tokens."""
+    import torch
+    from oracle import cpu_torch
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return
     from flashbfp_b200 import workloads
-    shapes = [(8192, 3840), (3840, 4096), (30720, 3840), (3840, 15360)]
-    rows = 256
-    samples = []
-    for i, (n, k) in enumerate(shapes):
-        dp, sp, rcv = _cpu_layer(n, k, seed=9000 + i, rows=rows)
-        X = np.random.default_rng(i).standard_normal((args.m, k)).astype(np.float32)
-        nbytes = 11 * dp["exponents"].size + 10 * sp["count"] + 2 * args.m * k + 2 * args.m * rows
-        samples.append((dp, rcv, X, nbytes))
+    layers = []
+    for i, (n, k) in enumerate([(8192, 3840), (3840, 4096), (30720, 3840), (3840, 15360)]):
+        W = workloads.decode_weight(n, k, seed=9000 + i)
+        dp, sp = cpu_torch.compress_matrix(W)
+        del W
+        rcv = cpu_torch.outlier_rcv(sp, dp["padded_shape"], n, k)
+        X = workloads.activations(args.m, k, seed=i)
+        layers.append((X, dp, rcv, cpu_torch.algorithmic_bytes_forward(dp, sp["count"], args.m, 2)))
+    step_bytes = sum(L[3] for L in layers)
 
-    def step(s):
-        dp, (r, c, v), X, _ = samples[s % len(samples)]
-        fallback_forward(X, dp["exponents"], dp["signs"], dp["payload"], dp["padded_shape"],
-                         dp["orig_shape"], r, c, v)
+    def step():
+        for X, dp, rcv, _ in layers:
+            cpu_torch.fallback_forward(X, dp, rcv)
 
-    for s in range(args.warmup):
-        step(s)
+    for _ in range(args.warmup):
+        step()
     t0 = time.perf_counter()
-    tot = 0
-    for s in range(args.steps):
-        step(s)
-        tot += samples[s % len(samples)][3]
+    for _ in range(args.steps):
+        step()
     el = time.perf_counter() - t0
-    val = tot / el / 1e9
+    val = step_bytes * args.steps / el / 1e9
     print(json.dumps({
         "impl": "reference", "metric": METRIC, "value": round(val, 4), "unit": "GB/s",
         "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": round(el * 1000 / args.steps, 4), "higher_is_better": True,
-        "scaling": "strong", "vs_baseline": None, "dtype": "fp32", "data": "synthetic",
-        "config": {"workload": f"reference CPU path (port) on 256-row samples of the 12B-class decode "
-                               f"linears, M={args.m}", "m": args.m, "parallelism": "host cores"},
-        "cpu_baseline": {"value": round(val, 4), "unit": "GB/s", "cores": _cpu_threads(), "kind": "port",
-                         "sample": "256 rows of each fused decode linear per step, rotating"},
+        "scaling": "strong", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+        "config": {"workload": f"reference CPU path on one 12B-class decoder layer per step (q|k|v 8192x3840, "
+                               f"o 3840x4096, gate|up 30720x3840, down 3840x15360), M={args.m}",
+                   "m": args.m, "parallelism": "host cores"},
+        "cpu_baseline": {"value": round(val, 4), "unit": "GB/s", "cores": cpu_torch.threads(), "kind": "port",
+                         "sample": "the four linears of one decoder layer per step, full size",
+                         "reference_over_port": _calibration()},
         "e2e": {"value": round(val, 4), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }), flush=True)
 

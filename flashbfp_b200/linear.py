@@ -40,13 +40,20 @@ def gemv_workspace(device: torch.device, npad: int) -> torch.Tensor:
 
 
 def check_device_errors(device=None) -> None:
-    """Synchronise and raise if a GEMV on `device` gave up a bounded device-side wait."""
+    """Synchronise and raise if a GEMV on `device` gave up a bounded device-side wait. The
+    workspace of a GEMV that gave up may hold partial sums and counters, so it is returned to
+    zero before the error is raised: later GEMVs on it are correct again."""
     L = _lib.lib()
     for (idx, sptr), ws in list(_WORKSPACES.items()):
         if device is not None and torch.device(device).index != idx:
             continue
         with torch.cuda.device(idx):
-            _lib.check(L.fbfp_gemv_check(_lib.ptr(ws), _lib.ctypes.c_void_p(sptr)), "fbfp_gemv_check")
+            try:
+                _lib.check(L.fbfp_gemv_check(_lib.ptr(ws), _lib.ctypes.c_void_p(sptr)), "fbfp_gemv_check")
+            except _lib.FlashBFPError:
+                ws.zero_()
+                torch.cuda.synchronize(idx)
+                raise
 
 
 GEMV_RESIDENT, GEMV_DENSE_ONLY, GEMV_TENSOR_CORES = 1, 4, 8

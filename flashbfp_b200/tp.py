@@ -131,6 +131,12 @@ class NVLinkAllReduce:
                         "fbfp_allreduce_sum_f32")
         return y
 
+    def set_timeout(self, timeout_s: float) -> None:
+        """Bound of every device-side wait on a peer's words, for this handle's all-reduce calls
+        and the GEMV exchanges fused with it (two seconds unless changed; 1 us .. 60 s)."""
+        self._lib.check(self._L.fbfp_allreduce_set_timeout(self._h, max(1, int(round(timeout_s * 1e6)))),
+                        "fbfp_allreduce_set_timeout")
+
     def check(self, device=None) -> None:
         """Synchronise and raise if a call gave up waiting for a rank."""
         dev = device if device is not None else torch.device("cuda", torch.cuda.current_device())

@@ -106,7 +106,8 @@ def run_case(ref, name, W: torch.Tensor, xs, bias_seed=None):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", default=os.environ.get("FLASHBFP_REFERENCE", "/root/reference"))
+    ap.add_argument("--reference", required=True,
+                    help="checkout of the reference project (the directory holding flash_bfp/)")
     args = ap.parse_args()
     sys.path.insert(0, args.reference)
     import flash_bfp  # noqa: F401

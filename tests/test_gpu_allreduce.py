@@ -102,7 +102,8 @@ def _fused_worker(rank, port, q):
         from flashbfp_b200 import build
         build.build()
         from flashbfp_b200 import OABFCompressor, packed, tp, workloads
-        from flashbfp_b200.linear import check_device_errors, packed_linear, packed_linear_allreduce
+        from flashbfp_b200.linear import (check_device_errors, gemv_records, gemv_workspace,
+                                          packed_linear, packed_linear_allreduce)
         from flashbfp_b200.tp import NVLinkAllReduce, TPLinear
         dev = torch.device("cuda", rank)
         ar = NVLinkAllReduce(40 * 3840)              # the separate path's 40-token reference
@@ -128,6 +129,8 @@ def _fused_worker(rank, port, q):
             pw = packed.from_compressed(dp, sp, dev)
             k0, k1 = tp.input_range(name, k, rank, WORLD)
             bias = (0.1 * torch.randn(n, generator=torch.Generator().manual_seed(5))).to(dev, torch.bfloat16)
+            pwr = packed.from_compressed(dp, sp, dev).build_records()
+            ws = gemv_workspace(dev, pwr.npad)
             for m in (1, 5, 16):
                 X = workloads.activations(m, k, seed=m, device=dev)
                 Xs = X[:, k0:k1]
@@ -138,6 +141,14 @@ def _fused_worker(rank, port, q):
                 assert rel(Yf, ref) <= 1e-5, (name, m, rel(Yf, ref))
                 assert rel(Yb, ref) <= 5e-3, (name, m, rel(Yb, ref))      # bf16 rounding of y
                 assert same_on_ranks(Yf) and same_on_ranks(Yb), (name, m)
+                # the stage-record GEMV with the same exchange fused in (one token on the CUDA
+                # cores and on the tensor cores; more on the tensor cores)
+                for tc in ((False, True) if m == 1 else (True,)):
+                    Yr = torch.empty(m, n, dtype=torch.float32, device=dev)
+                    gemv_records(Xs, pwr, Yr, ws, bias, reducer=ar, tensor_cores=tc)
+                    check_device_errors(dev)
+                    assert rel(Yr, ref) <= 1e-5, (name, m, tc, rel(Yr, ref))
+                    assert same_on_ranks(Yr), (name, m, tc)
             # the module path: 40 tokens = three fused launches (16 + 16 + 8)
             lin = TPLinear(pw, name, rank, WORLD, k, bias=bias, reducer=ar)
             X = workloads.activations(40, k, seed=40, device=dev)

@@ -310,6 +310,37 @@ def test_state_dict_reference_keys_and_roundtrip():
     assert torch.allclose(lin(X).float(), lin2(X).float(), rtol=1e-3, atol=1e-3)
 
 
+@pytest.mark.parametrize("name", CASES)
+def test_load_state_dict_assembled_from_reference_arrays(name):
+    """A state dict in the reference's own form (triton_kernel.py:232-291, 370-379): exponents as
+    fp32, signs and flattened payload as int32, outliers as int64 (input row, output column)
+    pairs with fp32 values, the fp32 `_sp_value` buffer, built from the fixture's arrays (not from
+    this package's compressor), loads (:381-423) and reproduces the reference's forward outputs."""
+    from flashbfp_b200 import OABFLinear
+    g = load(name)
+    n, k = g["orig_shape"]
+    has_bias = "bias" in g
+    sd = {"_dp_exponents": torch.from_numpy(g["exponents"].astype(np.float32)),
+          "_dp_signs": torch.from_numpy(g["signs"].astype(np.int32)),
+          "_dp_payload": torch.from_numpy(g["payload"].astype(np.int32).reshape(-1)),
+          "_sp_value": torch.from_numpy(g["value"].astype(np.float32))}
+    if g["count"]:
+        sd.update({"_sp_r_idx": torch.from_numpy(g["r_idx"].astype(np.int64)),
+                   "_sp_c_idx": torch.from_numpy(g["c_idx"].astype(np.int64)),
+                   "_sp_v_val": torch.from_numpy(g["v_val"].astype(np.float32))})
+    if has_bias:
+        sd["bias"] = torch.from_numpy(g["bias"].astype(np.float32))
+    lin = OABFLinear(k, n, bias=has_bias).cuda()
+    lin.load_state_dict(sd)
+    for X, xdt, Yref in g["xs"]:
+        Xt = torch.from_numpy(X).to(torch.bfloat16 if xdt == "bf16" else torch.float32).cuda()
+        Y = lin(Xt)
+        assert Y.shape == Yref.shape
+        assert oabf.rel_l2(Y.float().cpu().numpy(), Yref) <= GEMM_TOL
+        exact = _oracle_linear_np(g, Xt.float().cpu().numpy(), g.get("bias"))
+        assert oabf.rel_l2(Y.float().cpu().numpy(), exact) <= GEMM_TOL
+
+
 def test_errors_fail_loudly():
     from flashbfp_b200 import OABFCompressor, OABFLinear
     lin = OABFLinear(32, 64, bias=False)
