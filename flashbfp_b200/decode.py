@@ -25,7 +25,7 @@ from typing import List, Optional, Sequence
 import torch
 
 from . import _lib
-from .linear import packed_linear
+from .linear import packed_linear, packed_linear_allreduce
 from .packed import PackedWeight, concat_rows
 
 
@@ -47,6 +47,8 @@ class DecoderShape:
 
 @dataclass
 class DecodeLayer:
+    """One decoder layer's weights: OABF PackedWeights (or, for the uncompressed baseline,
+    dense bf16 [N, K] tensors in their place)."""
     qkv: PackedWeight                     # q | k | v rows
     o: PackedWeight
     gate_up: PackedWeight                 # gate | up rows
@@ -57,6 +59,14 @@ class DecodeLayer:
     post_ffn_ln: torch.Tensor
     q_norm: torch.Tensor
     k_norm: torch.Tensor
+
+
+def _dims(w) -> tuple:
+    """(rows, columns) of a layer weight: a PackedWeight, or a dense bf16 [N, K] tensor (the
+    uncompressed baseline decoder)."""
+    if isinstance(w, PackedWeight):
+        return w.n_out, w.k_in
+    return int(w.shape[0]), int(w.shape[1])
 
 
 def rope_tables(theta: float, head_dim: int, max_ctx: int, device) -> tuple:
@@ -70,52 +80,83 @@ def rope_tables(theta: float, head_dim: int, max_ctx: int, device) -> tuple:
 
 
 class GemmaDecoder:
+    """One rank's decoder. Without ``reducer`` the layers hold whole matrices. With ``reducer``
+    (an ``NVLinkAllReduce`` over the tensor-parallel ranks) they hold this rank's parts as
+    ``tp.DecoderPlan`` splits them: q|k|v rows of its heads, o_proj input columns of its heads,
+    gate|up rows and down_proj input columns of its intermediate range; ``lm_head`` holds its
+    vocabulary rows starting at ``vocab_offset``. The row-parallel sums run inside the o_proj
+    and down_proj GEMVs, the residual stream and norms are replicated (identical bits on every
+    rank), and the greedy pick gathers each rank's (max logit, index) through the same
+    reducer."""
+
     def __init__(self, shape: DecoderShape, layers: List[DecodeLayer], embed: torch.Tensor,
                  final_norm: torch.Tensor, lm_head: torch.Tensor, max_ctx: int, device=None,
-                 max_prefill: int = 128):
+                 max_prefill: int = 128, reducer=None, vocab_offset: int = 0):
         self.L = _lib.lib()
         self.shape, self.layers = shape, layers
         dev = torch.device(device) if device is not None else embed.device
         self.device = dev
         s = shape
+        self.reducer = reducer
+        self.world = reducer.world if reducer is not None else 1
+        self.rank = reducer.rank if reducer is not None else 0
         if len(layers) != len(s.layer_types):
             raise ValueError(f"{len(layers)} layers but {len(s.layer_types)} layer types")
         if s.head_dim % 8 or s.head_dim > 256 or max_ctx + 8 * s.head_dim > 10000:
             raise ValueError("head_dim must be a multiple of 8 up to 256, and max_ctx + 8 * head_dim "
                              "at most 10000")
-        q_rows = (s.n_heads + 2 * s.n_kv_heads) * s.head_dim
+        if s.n_heads % self.world or s.n_kv_heads % self.world:
+            raise ValueError(f"heads ({s.n_heads} / {s.n_kv_heads}) do not split over {self.world} ranks")
+        self.hq, self.hkv = s.n_heads // self.world, s.n_kv_heads // self.world
+        self.inter_l = _dims(layers[0].gate_up)[0] // 2 if layers else s.inter
+        q_rows = (self.hq + 2 * self.hkv) * s.head_dim
         for i, ly in enumerate(layers):
             # the fused rows must hold the heads back to back (each part's rows a multiple of 64)
-            if ly.qkv.n_out != q_rows or ly.gate_up.n_out != 2 * s.inter or ly.o.n_out != s.hidden \
-                    or ly.down.n_out != s.hidden:
-                raise ValueError(f"layer {i}: fused row counts do not match the shape "
-                                 f"(q|k|v {ly.qkv.n_out} vs {q_rows}, gate|up {ly.gate_up.n_out} vs "
-                                 f"{2 * s.inter})")
+            (nq, _), (ngu, _), (no, ko), (nd, kd) = (_dims(ly.qkv), _dims(ly.gate_up), _dims(ly.o),
+                                                     _dims(ly.down))
+            if nq != q_rows or ngu != 2 * self.inter_l or no != s.hidden or nd != s.hidden \
+                    or ko != self.hq * s.head_dim or kd != self.inter_l:
+                raise ValueError(f"layer {i}: row / column counts do not match the shape on "
+                                 f"{self.world} rank(s) (q|k|v {nq} vs {q_rows}, gate|up {ngu} vs "
+                                 f"{2 * self.inter_l}, o in {ko}, down in {kd})")
+        if self.world == 1 and self.inter_l != s.inter:
+            raise ValueError(f"gate|up holds {2 * self.inter_l} rows, not {2 * s.inter}")
         self.max_ctx = int(max_ctx)
         bf = dict(dtype=torch.bfloat16, device=dev)
         self.embed = embed.to(**bf).contiguous()
         self.final_norm = final_norm.to(**bf).contiguous()
         self.lm_head = lm_head.to(**bf).contiguous()
+        self.vocab_offset = int(vocab_offset)
+        self.vocab_l = self.lm_head.shape[0]
         self.embed_scale = float(s.hidden) ** 0.5
         self.scaling = float(s.query_pre_attn_scalar) ** -0.5
         self.rope = {
             "sliding_attention": rope_tables(s.rope_theta_local, s.head_dim, self.max_ctx, dev),
             "full_attention": rope_tables(s.rope_theta_global, s.head_dim, self.max_ctx, dev),
         }
-        cache = (len(layers), s.n_kv_heads, self.max_ctx, s.head_dim)
+        cache = (len(layers), self.hkv, self.max_ctx, s.head_dim)
         self.k_cache = torch.zeros(cache, **bf)
         self.v_cache = torch.zeros(cache, **bf)
         R = self.max_rows = max(1, int(max_prefill))         # rows of a prompt chunk
         self.h = torch.zeros(R, s.hidden, **bf)              # residual stream
         self.x = torch.zeros(R, s.hidden, **bf)              # normalised input of the next linear
         self.qkv = torch.zeros(R, q_rows, **bf)
-        self.q = torch.zeros(R, s.n_heads * s.head_dim, **bf)
-        self.attn = torch.zeros(R, s.n_heads * s.head_dim, **bf)
+        self.q = torch.zeros(R, self.hq * s.head_dim, **bf)
+        self.attn = torch.zeros(R, self.hq * s.head_dim, **bf)
         self.o = torch.zeros(R, s.hidden, **bf)
-        self.gu = torch.zeros(R, 2 * s.inter, **bf)
-        self.act = torch.zeros(R, s.inter, **bf)
+        self.gu = torch.zeros(R, 2 * self.inter_l, **bf)
+        self.act = torch.zeros(R, self.inter_l, **bf)
         self.down = torch.zeros(R, s.hidden, **bf)
-        self.logits = torch.zeros(1, s.vocab, **bf)
+        self.logits = torch.zeros(1, self.vocab_l, **bf)     # this rank's vocabulary rows
+        if reducer is not None:
+            from .linear import fused_shard_eligible
+            if reducer.max_elems < max(R * s.hidden, 2 * self.world):
+                raise ValueError(f"the reducer holds {reducer.max_elems} values; a prompt chunk of "
+                                 f"{R} rows needs {R * s.hidden}")
+            self.fused_rows = all(fused_shard_eligible(pw, reducer.max_elems)
+                                  for ly in layers for pw in (ly.o, ly.down))
+            self.pick = torch.zeros(2 * self.world, dtype=torch.float32, device=dev)
+            self.row_f32 = torch.zeros(R, s.hidden, dtype=torch.float32, device=dev)
         self.tok = torch.zeros(R, dtype=torch.int64, device=dev)   # ids in; tok[0] = next token
         self.pos = torch.zeros(1, dtype=torch.int32, device=dev)
         self.err = torch.zeros(1, dtype=torch.int32, device=dev)
@@ -124,7 +165,11 @@ class GemmaDecoder:
 
     # -- construction from a Hugging Face Gemma-3 model after compress_gemma_model -----------
     @classmethod
-    def from_hf(cls, model, max_ctx: int, device=None, max_prefill: int = 128) -> "GemmaDecoder":
+    def from_hf(cls, model, max_ctx: int, device=None, max_prefill: int = 128,
+                reducer=None) -> "GemmaDecoder":
+        """The decoder of a Gemma-3 causal LM after ``compress_gemma_model``; with ``reducer``,
+        of a model compressed with ``compress_gemma_model(..., rank=r, world=reducer.world)``
+        on every rank (this rank's shards; lm_head rows split here)."""
         cfg = model.config
         if getattr(cfg, "final_logit_softcapping", None) or getattr(cfg, "attn_logit_softcapping", None):
             raise NotImplementedError("logit soft-capping is not supported")
@@ -160,12 +205,56 @@ class GemmaDecoder:
         for ly in layers:
             for f in ("input_ln", "post_attn_ln", "pre_ffn_ln", "post_ffn_ln", "q_norm", "k_norm"):
                 setattr(ly, f, getattr(ly, f).to(device=dev, dtype=torch.bfloat16).contiguous())
+        lm_head, v0 = model.lm_head.weight.data, 0
+        if reducer is not None:
+            from .tp import DecoderPlan
+            plan = DecoderPlan.from_config(cfg, reducer.rank, reducer.world)
+            for i, lyr in enumerate(inner.layers):
+                if getattr(lyr.self_attn.o_proj, "tp_range", None) != plan.q_rows or \
+                        getattr(lyr.mlp.down_proj, "tp_range", None) != plan.inter:
+                    raise ValueError(f"layer {i} was not compressed for rank {reducer.rank} of "
+                                     f"{reducer.world} (compress_gemma_model(..., rank, world))")
+            v0, v1 = plan.vocab
+            lm_head = lm_head[v0:v1]
+        elif any(hasattr(m, "tp_mode") for m in model.modules()):
+            raise ValueError("the model holds tensor-parallel shards: pass the reducer")
         return cls(shape, layers, inner.embed_tokens.weight.data, inner.norm.weight.data,
-                   model.lm_head.weight.data, max_ctx, dev, max_prefill)
+                   lm_head, max_ctx, dev, max_prefill, reducer=reducer, vocab_offset=v0)
 
     # -- one token ---------------------------------------------------------------------------
-    def _linear(self, x: torch.Tensor, pw: PackedWeight, out: torch.Tensor) -> None:
-        packed_linear(x, pw, None, torch.bfloat16, out=out)
+    def _linear(self, x: torch.Tensor, pw, out: torch.Tensor) -> None:
+        if isinstance(pw, PackedWeight):
+            packed_linear(x, pw, None, torch.bfloat16, out=out)
+        else:                                                 # a dense bf16 weight (baseline)
+            torch.matmul(x, pw.t(), out=out)
+
+    def _row_linear(self, x: torch.Tensor, pw, out: torch.Tensor) -> None:
+        """o_proj / down_proj: on several ranks the sum of the ranks' partial products, fused
+        into the GEMV for decode-sized chunks, else a separate peer-memory all-reduce."""
+        if self.reducer is None:
+            self._linear(x, pw, out)
+            return
+        m = x.shape[0]
+        if self.fused_rows and m <= 64:
+            packed_linear_allreduce(x, pw, self.reducer, None, torch.bfloat16, out=out)
+        else:
+            y = self.row_f32[:m]
+            packed_linear(x, pw, None, torch.float32, out=y)
+            self.reducer(y)
+            out.copy_(y)
+
+    def _pick(self, m: int) -> None:
+        """Greedy token of the last row's logits into self.tok[0]: argmax over this rank's
+        vocabulary rows, then (several ranks) every rank's (max, index) gathered through the
+        reducer (a sum of one-hot slots is exact) and the first maximum taken."""
+        if self.reducer is None:
+            self.tok[:1].copy_(torch.argmax(self.logits, dim=-1))
+            return
+        from .tp import argmax_pick, argmax_slots
+        self.pick.zero_()
+        argmax_slots(self.logits, self.vocab_offset, self.rank, self.world, self.pick)
+        self.reducer(self.pick)
+        self.tok[:1].copy_(argmax_pick(self.pick))
 
     def _enqueue(self, m: int) -> None:
         """Rows 0..m-1 (tokens self.tok[:m] at positions self.pos ..): every layer, then the
@@ -184,24 +273,24 @@ class GemmaDecoder:
             cos_t, sin_t = self.rope[kind]
             window = s.sliding_window if kind == "sliding_attention" else 0
             self._linear(x, ly.qkv, qkv)
-            _lib.check(L.fbfp_qk_rope_cache(P(qkv), m, s.n_heads, s.n_kv_heads, s.head_dim, P(ly.q_norm),
+            _lib.check(L.fbfp_qk_rope_cache(P(qkv), m, self.hq, self.hkv, s.head_dim, P(ly.q_norm),
                                             P(ly.k_norm), eps, P(cos_t), P(sin_t), P(self.pos), self.max_ctx,
                                             P(q), P(self.k_cache[li]), P(self.v_cache[li]), P(self.err), st),
                        "fbfp_qk_rope_cache")
-            _lib.check(L.fbfp_decode_attention(P(q), m, P(self.k_cache[li]), P(self.v_cache[li]), s.n_heads,
-                                               s.n_kv_heads, s.head_dim, self.max_ctx, P(self.pos), window,
+            _lib.check(L.fbfp_decode_attention(P(q), m, P(self.k_cache[li]), P(self.v_cache[li]), self.hq,
+                                               self.hkv, s.head_dim, self.max_ctx, P(self.pos), window,
                                                self.scaling, P(attn), st), "fbfp_decode_attention")
-            self._linear(attn, ly.o, o)
+            self._row_linear(attn, ly.o, o)
             _lib.check(L.fbfp_post_residual_norm(P(o), m, P(ly.post_attn_ln), P(h), P(ly.pre_ffn_ln), eps,
                                                  s.hidden, P(x), st), "fbfp_post_residual_norm")
             self._linear(x, ly.gate_up, gu)
-            _lib.check(L.fbfp_geglu(P(gu), m, s.inter, P(act), st), "fbfp_geglu")
-            self._linear(act, ly.down, down)
+            _lib.check(L.fbfp_geglu(P(gu), m, self.inter_l, P(act), st), "fbfp_geglu")
+            self._row_linear(act, ly.down, down)
             nxt = self.layers[li + 1].input_ln if li + 1 < len(self.layers) else self.final_norm
             _lib.check(L.fbfp_post_residual_norm(P(down), m, P(ly.post_ffn_ln), P(h), P(nxt), eps,
                                                  s.hidden, P(x), st), "fbfp_post_residual_norm")
         torch.matmul(x[m - 1:m], self.lm_head.t(), out=self.logits)     # bf16 lm_head (cuBLAS)
-        self.tok[:1].copy_(torch.argmax(self.logits, dim=-1))
+        self._pick(m)
         _lib.check(L.fbfp_advance_position(P(self.pos), m, st), "fbfp_advance_position")
 
     def _enqueue_step(self) -> None:

@@ -80,6 +80,84 @@ def slice_packed(pw: packed.PackedWeight, name: str, rank: int, world: int,
     return packed.shard_cols(pw, c0 // 16, (c1 + 15) // 16, tiles=tiles)
 
 
+class DecoderPlan:
+    """How a decoder's weights split over `world` ranks (whole-model tensor parallelism).
+
+    * attention: whole heads. Rank r holds query heads [r*hq, (r+1)*hq) and KV heads
+      [r*hkv, (r+1)*hkv) (hq = n_heads / world, hkv = n_kv_heads / world): its q/k/v rows, its
+      KV cache, and the matching input columns of o_proj (row-parallel);
+    * MLP: the intermediate dimension in whole 256-column stages, the same range for the rows of
+      gate_proj and up_proj (column-parallel) and the input columns of down_proj (row-parallel);
+    * lm_head: vocabulary rows in units of 64 (vocab-parallel logits, local argmax).
+    Embeddings and norms are replicated."""
+
+    def __init__(self, n_heads: int, n_kv_heads: int, head_dim: int, inter: int, vocab: int,
+                 rank: int, world: int):
+        if n_heads % world or n_kv_heads % world:
+            raise ValueError(f"{n_heads} query / {n_kv_heads} KV heads do not split over {world} ranks")
+        if not 0 <= rank < world:
+            raise ValueError(f"rank {rank} outside world {world}")
+        self.rank, self.world, self.head_dim = rank, world, head_dim
+        self.hq, self.hkv = n_heads // world, n_kv_heads // world
+        self.q_rows = (rank * self.hq * head_dim, (rank + 1) * self.hq * head_dim)
+        self.kv_rows = (rank * self.hkv * head_dim, (rank + 1) * self.hkv * head_dim)
+        self.inter = split(inter, rank, world, align=ROW_K_ALIGN)
+        self.vocab = split(vocab, rank, world, align=64)
+
+    @classmethod
+    def from_config(cls, cfg, rank: int, world: int) -> "DecoderPlan":
+        head_dim = getattr(cfg, "head_dim", None) or cfg.hidden_size // cfg.num_attention_heads
+        return cls(cfg.num_attention_heads, cfg.num_key_value_heads, head_dim, cfg.intermediate_size,
+                   cfg.vocab_size, rank, world)
+
+    def ranges(self, name: str) -> Tuple[str, int, int]:
+        """(mode, lo, hi) of this rank's part of linear `name`: output rows [lo, hi) for
+        'column', input columns [lo, hi) for 'row'."""
+        base = name.rsplit(".", 1)[-1]
+        if base == "q_proj":
+            return ("column",) + self.q_rows
+        if base in ("k_proj", "v_proj"):
+            return ("column",) + self.kv_rows
+        if base == "o_proj":
+            return ("row",) + self.q_rows
+        if base in ("gate_proj", "up_proj"):
+            return ("column",) + self.inter
+        if base == "down_proj":
+            return ("row",) + self.inter
+        raise ValueError(f"no tensor-parallel split for {name!r}")
+
+    def slice(self, W: torch.Tensor, name: str) -> torch.Tensor:
+        mode, lo, hi = self.ranges(name)
+        return W[lo:hi] if mode == "column" else W[:, lo:hi]
+
+    def compress(self, W: torch.Tensor, name: str, compressor):
+        """(dense_payload, sparse_outliers) of this rank's part of W, with the whole matrix's
+        outlier threshold (so its bytes equal that part of the whole matrix's compression)."""
+        thr = compressor.compute_dynamic_threshold(W)
+        return compressor.compress_matrix_device(self.slice(W, name).contiguous(), threshold=thr)
+
+
+def argmax_slots(logits: torch.Tensor, vocab_offset: int, rank: int, world: int,
+                 slots: torch.Tensor) -> None:
+    """Vocab-parallel greedy pick, first half: write this rank's (max logit, global index of its
+    first maximum) into slots [2 rank, 2 rank + 2) of the zeroed fp32 vector ``slots`` (2 world
+    values). Summing the ranks' vectors (any all-reduce) then gathers every rank's pair exactly:
+    each slot has one non-zero contributor, and indices below 2^24 are exact in fp32."""
+    val, idx = torch.max(logits.reshape(-1).float(), dim=0)
+    slots[2 * rank:2 * rank + 1].copy_(val.reshape(1))
+    slots[2 * rank + 1:2 * rank + 2].copy_((idx + vocab_offset).float().reshape(1))
+
+
+def argmax_pick(slots: torch.Tensor) -> torch.Tensor:
+    """Second half: the global index (int64, shape [1]) of the largest of the gathered maxima,
+    the lowest rank's on ties, which is the first maximum over the whole vocabulary because the
+    ranks hold ascending vocabulary ranges."""
+    pairs = slots.view(-1, 2)
+    # index_select keeps the pick on the device (indexing by a 0-d tensor would read it back
+    # to the host, which a CUDA graph capture does not allow)
+    return pairs[:, 1].index_select(0, torch.argmax(pairs[:, 0]).reshape(1)).long()
+
+
 def all_reduce_sum(y: torch.Tensor, group=None, reducer: Optional["NVLinkAllReduce"] = None) -> torch.Tensor:
     """Sum of the ranks' fp32 partial outputs (row-parallel exchange), in place: through the
     NVLink peer-memory reducer when one is given, else the process group's all-reduce."""
