@@ -60,6 +60,7 @@ def parse():
                          "over NVLink peer memory, a separate NVLink all-reduce kernel, or NCCL")
     ap.add_argument("--no-model", action="store_true",
                     help="skip the full-model decode token step (N = 1 only)")
+    ap.add_argument("--no-70b", action="store_true", help="skip the 70B-class stress section")
     ap.add_argument("--no-prefill", action="store_true",
                     help="skip the prefill GEMM and the bf16 cuBLAS decode baseline")
     return ap.parse_args()
@@ -131,17 +132,26 @@ def _progress(rank, msg):
         print(f"[rank {rank}] {time.strftime('%H:%M:%S')} {msg}", file=sys.stderr, flush=True)
 
 
-def build_layers(n_layers, rank, world, device):
+GEMMA12B = dict(n_heads=16, n_kv_heads=8, head_dim=256, inter=15360, vocab=262144, hidden=3840)
+
+
+def build_layers(n_layers, rank, world, device, shapes=None, plan_args=None, frac=0.015, seed0=1000):
+    """Every linear of n_layers decoder layers, this rank's part as the whole-model tensor-parallel
+    plan splits it (whole heads; the MLP in 256-column stages), compressed on the GPU."""
     from flashbfp_b200 import OABFCompressor, packed, tp, workloads
     comp = OABFCompressor(16, 64)
+    shapes = shapes or workloads.GEMMA12B_LAYER
+    pa = plan_args or GEMMA12B
+    plan = tp.DecoderPlan(pa["n_heads"], pa["n_kv_heads"], pa["head_dim"], pa["inter"], pa["vocab"],
+                          rank, world)
     layers = []
     shard_bytes = {k: 0 for k in KINDS}
     for li in range(n_layers):
         parts = {}
-        for j, (name, (n, k)) in enumerate(workloads.GEMMA12B_LAYER.items()):
-            W = workloads.decode_weight(n, k, seed=1000 + 16 * li + j, device=device)
-            # this rank's slice, compressed with the whole matrix's threshold
-            dp, sp = tp.compress_shard(W, name, rank, world, comp)
+        for j, (name, (n, k)) in enumerate(shapes.items()):
+            W = workloads.decode_weight(n, k, seed=seed0 + 16 * li + j, frac=frac, device=device)
+            # this rank's part, compressed with the whole matrix's threshold
+            dp, sp = plan.compress(W, name, comp)
             parts[name] = packed.from_compressed(dp, sp, device, build_tiles=False)
             del W, dp, sp
         L = {
@@ -340,14 +350,18 @@ def run_ours(args):
         e2e = run_e2e(args, layers, xs, stream, device, world, rank, step_bytes, exchange, reducer, fused)
 
     model = None
-    if world == 1 and m == 1 and not args.no_model:
-        try:
-            model = run_model_decode(layers, device)
-        except Exception as e:                  # reported on the line; the headline stands
-            model = {"error": f"{type(e).__name__}: {e}"[:300]}
+    if m == 1 and not args.no_model:
+        _progress(rank, "model decode")
+        model = run_models(layers, device, rank, world)
 
-    prefill = bf16 = compress = None
+    stress = None
+    if not args.no_70b:
+        _progress(rank, "70B-class stress")
+        stress = run_stress70b(device, rank, world)
+
+    prefill = bf16 = compress = sweep = None
     if world == 1 and not args.no_prefill:
+        sweep = run_decode_sweep(layers, device)
         prefill = run_prefill(layers, device)
         bf16 = run_bf16_decode(device, m=m)
         compress = run_compress(device)
@@ -400,6 +414,8 @@ def run_ours(args):
             "gpu_launches": 4 * args.layers * K,
             "e2e": e2e,
             "model_decode": model,
+            "decode_sweep": sweep,
+            "stress_70b": stress,
             "prefill": prefill,
             "bf16_cublas_decode": bf16,
             "compress": compress,
@@ -520,17 +536,13 @@ def run_e2e(args, layers, xs, stream, device, world, rank, step_bytes, exchange,
             "steps": K, "api": "OABFLinear.forward in a CUDA graph"}
 
 
-def run_prefill(layers, device, m=2048, iters=10):
-    """Prefill GEMM (tensor-bound): the gate|up linear of layer 0 at m bf16 tokens, through
-    packed_linear (fbfp_gemm_prefill), beside cuBLAS bf16 on a dense bf16 weight of the same
-    shape. CUDA events on the launching stream; 3 warm-up launches."""
+def run_prefill(layers, device, ms=(512, 2048, 8192), iters=5):
+    """Prefill GEMM (tensor-bound): the gate|up (30720x3840) and down (3840x15360) linears of
+    layer 0 at M bf16 tokens through packed_linear (fbfp_gemm_prefill), beside cuBLAS bf16 on a
+    dense bf16 weight of the same shape. CUDA events on the launching stream; 3 warm-up launches."""
     from flashbfp_b200 import workloads
     from flashbfp_b200.linear import packed_linear, check_device_errors
-    pw = layers[0]["gate_up"]
-    X = workloads.activations(m, pw.k_in, seed=11, device=device)
-    Y = torch.empty(m, pw.n_out, dtype=torch.bfloat16, device=device)
-    Wb = (torch.randn(pw.n_out, pw.k_in, device=device) * 0.02).to(torch.bfloat16)
-    flops = 2.0 * m * pw.n_out * pw.k_in
+    peaks = _peaks()
 
     def timed(fn):
         for _ in range(3):
@@ -544,18 +556,32 @@ def run_prefill(layers, device, m=2048, iters=10):
         torch.cuda.synchronize(device)
         return a.elapsed_time(b) / iters
 
-    ms = timed(lambda: packed_linear(X, pw, out=Y))
-    check_device_errors(device)
-    ms_b = timed(lambda: torch.matmul(X, Wb.t()))
-    peaks = _peaks()
-    tf = flops / (ms * 1e-3) / 1e12
-    return {"workload": f"prefill: gate|up {pw.n_out}x{pw.k_in} OABF at M={m} bf16 tokens",
-            "m": m, "ms": round(ms, 4), "tflops": round(tf, 1),
-            "roofline": {"bound": "tensor", "achieved": round(tf, 1), "peak": peaks["bf16_tflops"],
-                         "unit": "TFLOP/s", "frac": round(tf / peaks["bf16_tflops"], 4),
-                         "peak_source": peaks["source"], "kernel": "prefill_tc_kernel"},
-            "cublas_bf16_tflops": round(flops / (ms_b * 1e-3) / 1e12, 1),
-            "cublas_bf16_note": "torch.matmul on a dense bf16 weight of the same shape (uncompressed)"}
+    rows = []
+    for kk in ("gate_up", "down"):
+        pw = layers[0][kk]
+        Wb = (torch.randn(pw.n_out, pw.k_in, device=device) * 0.02).to(torch.bfloat16)
+        for m in ms:
+            X = workloads.activations(m, pw.k_in, seed=11, device=device)
+            Y = torch.empty(m, pw.n_out, dtype=torch.bfloat16, device=device)
+            flops = 2.0 * m * pw.n_out * pw.k_in
+            ms_ = timed(lambda: packed_linear(X, pw, out=Y))
+            check_device_errors(device)
+            ms_b = timed(lambda: torch.matmul(X, Wb.t()))
+            tf = flops / (ms_ * 1e-3) / 1e12
+            rows.append({"linear": f"{kk} {pw.n_out}x{pw.k_in}", "m": m, "ms": round(ms_, 4),
+                         "tflops": round(tf, 1), "frac": round(tf / peaks["bf16_tflops"], 4),
+                         "cublas_bf16_tflops": round(flops / (ms_b * 1e-3) / 1e12, 1)})
+            del X, Y
+        del Wb
+    head = next(r for r in rows if r["m"] == 2048 and r["linear"].startswith("gate_up"))
+    return {"workload": "prefill: OABF gate|up and down linears at M = 512, 2048, 8192 bf16 tokens",
+            "m": 2048, "ms": head["ms"], "tflops": head["tflops"],
+            "roofline": {"bound": "tensor", "achieved": head["tflops"], "peak": peaks["bf16_tflops"],
+                         "unit": "TFLOP/s", "frac": head["frac"], "peak_source": peaks["source"],
+                         "kernel": "prefill_tc_kernel (gate|up at M=2048)"},
+            "cublas_bf16_tflops": head["cublas_bf16_tflops"],
+            "cublas_bf16_note": "torch.matmul on a dense bf16 weight of the same shape (uncompressed)",
+            "sizes": rows}
 
 
 def run_compress(device, iters=5):
@@ -583,12 +609,12 @@ def run_compress(device, iters=5):
             "algorithmic_gbs": round(alg / (ms * 1e-3) / 1e9, 1), "outliers": int(sp["count"])}
 
 
-def run_model_decode(layers, device, prompt=128, gen=256):
-    """Whole decode tokens of a random-init 12B-class Gemma-3 (the benchmark's OABF layers, 5
+def _decoder(layers, device, reducer, rank, world, batch, prompt, gen):
+    """The random-init 12B-class Gemma-3 around the given layers (this rank's parts): 5
     sliding-window layers of 1024 per global one, 16 query / 8 key-value heads of 256, bf16
-    embedding and lm_head of 262144 x 3840): the ``prompt`` tokens as one prefill chunk (timed
-    on its own), then ``gen`` greedy tokens timed as back-to-back replays of the one-token CUDA
-    graph."""
+    embedding and lm_head of 262144 x 3840 (this rank's vocabulary rows). The layers hold
+    PackedWeights, or bf16 tensors for the uncompressed baseline."""
+    from flashbfp_b200 import tp
     from flashbfp_b200.decode import DecodeLayer, DecoderShape, GemmaDecoder
     H, I, NH, NKV, HD, V = 3840, 15360, 16, 8, 256, 262144
     n = len(layers)
@@ -604,42 +630,306 @@ def run_model_decode(layers, device, prompt=128, gen=256):
                        input_ln=rnd(H, scale=0.1), post_attn_ln=rnd(H, scale=0.1),
                        pre_ffn_ln=rnd(H, scale=0.1), post_ffn_ln=rnd(H, scale=0.1),
                        q_norm=rnd(HD, scale=0.1), k_norm=rnd(HD, scale=0.1)) for Ly in layers]
-    dec = GemmaDecoder(shape, dls, rnd(V, H, scale=0.02), rnd(H, scale=0.1), rnd(V, H, scale=0.02),
-                       max_ctx=prompt + gen + 1, device=device)
+    embed, final = rnd(V, H, scale=0.02), rnd(H, scale=0.1)
+    v0, v1 = tp.DecoderPlan(NH, NKV, HD, I, V, rank, world).vocab
+    lm_head = rnd(V, H, scale=0.02)[v0:v1].clone()
+    return GemmaDecoder(shape, dls, embed, final, lm_head, max_ctx=prompt + gen + 1, device=device,
+                        max_prefill=prompt, reducer=reducer, vocab_offset=v0, batch=batch)
+
+
+def run_model_decode(layers, device, reducer=None, rank=0, world=1, batch=1, prompt=128, gen=256,
+                     dense=False):
+    """Whole decode tokens of the random-init 12B-class Gemma-3: every sequence's ``prompt``
+    tokens as one prefill chunk (timed on its own), then ``gen`` greedy tokens for all ``batch``
+    sequences together, timed as back-to-back replays of the one-step CUDA graph (max over
+    ranks)."""
+    import torch.distributed as dist
+    dec = _decoder(layers, device, reducer, rank, world, batch, prompt, gen)
     dec.capture()
-    ids = torch.randint(0, V, (prompt,), generator=torch.Generator().manual_seed(5)).tolist()
+    gids = torch.Generator().manual_seed(5)
+    prompts = [torch.randint(0, 262144, (prompt,), generator=gids).tolist() for _ in range(batch)]
     dec.reset(0)
-    dec.prefill(ids)                            # warm-up of the prompt path, then timed
+    dec.prefill(prompts[0])                     # warm-up of the prompt path, then timed
     dec.reset(0)
-    pa, pb = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     dec.stream.synchronize()
+    if world > 1:
+        dist.barrier()
+    pa, pb = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     pa.record(dec.stream)
-    dec.prefill(ids)
+    for b, p in enumerate(prompts):
+        dec.prefill(p, seq=b)
     pb.record(dec.stream)
-    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     dec.stream.synchronize()
     prefill_ms = pa.elapsed_time(pb)
+    a, b_ = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     a.record(dec.stream)
     for _ in range(gen):
         dec.step()
-    b.record(dec.stream)
+    b_.record(dec.stream)
     dec.check()
-    ms = a.elapsed_time(b) / gen
-    packed = sum(Ly[kk].packed_bytes() for Ly in layers for kk in KINDS)
-    per_token = packed + 2 * V * H + 2 * H        # OABF linears, bf16 lm_head, one embedding row
+    ms = a.elapsed_time(b_) / gen
+    t = torch.tensor([ms, prefill_ms], dtype=torch.float64, device=device)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms, prefill_ms = float(t[0]), float(t[1])
+    if dense:
+        lin = sum(2 * Ly[kk].numel() for Ly in layers for kk in KINDS)      # bf16 tensors
+    else:
+        lin = sum(Ly[kk].packed_bytes() for Ly in layers for kk in KINDS)
+    H = 3840
+    per_rank = lin + 2 * dec.vocab_l * H + 2 * batch * H      # linears, lm_head rows, embedding rows
     dec.release()
     del dec
     torch.cuda.empty_cache()
-    return {"workload": (f"random-init 12B-class Gemma-3 decode: {n} layers (5 sliding-window "
+    return {"workload": (f"random-init 12B-class Gemma-3 decode: {len(layers)} layers (5 sliding-window "
                          "layers of 1024 per global one), 16 q / 8 kv heads x 256, vocab 262144, "
-                         f"{prompt} prompt tokens then {gen} greedy tokens, batch 1"),
-            "ms_per_token": round(ms, 4), "tokens_per_s": round(1000.0 / ms, 1),
+                         f"{prompt} prompt tokens then {gen} greedy tokens, batch {batch}, "
+                         f"{'tp%d' % world if world > 1 else '1 GPU'}"
+                         + (", uncompressed bf16 linears (cuBLAS)" if dense else ", OABF linears")),
+            "batch": batch, "ms_per_step": round(ms, 4),
+            "tokens_per_s": round(batch * 1000.0 / ms, 1),
             "prefill_ms": round(prefill_ms, 3),
-            "prefill_tokens_per_s": round(prompt * 1000.0 / prefill_ms, 1),
-            "weight_gbs": round(per_token / (ms * 1e-3) / 1e9, 1),
-            "bytes_per_token": per_token,
-            "graph": "one CUDA graph per token: OABF GEMVs, decode.cu kernels, bf16 lm_head, argmax",
-            "lm_head": "uncompressed bf16 262144x3840 through cuBLAS (left alone by the model surgery)"}
+            "prefill_tokens_per_s": round(batch * prompt * 1000.0 / prefill_ms, 1),
+            "weight_gbs_per_rank": round(per_rank / (ms * 1e-3) / 1e9, 1),
+            "weight_bytes_per_rank": per_rank,
+            "graph": "one CUDA graph per step: linears, decode.cu kernels, bf16 lm_head, greedy pick",
+            "lm_head": "uncompressed bf16 through cuBLAS (left alone by the model surgery)"}
+
+
+def run_models(layers, device, rank, world):
+    """Whole-model decode at batch 1 and 8 (tensor-parallel over the ranks), and at one GPU the
+    same decoder on uncompressed bf16 linears, with the speed-up over it."""
+    out = {}
+    dred = None
+    if world > 1:
+        from flashbfp_b200.tp import NVLinkAllReduce
+        dred = NVLinkAllReduce(128 * 3840)          # a 128-token prompt chunk of the residual stream
+    for key, batch in (("batch1", 1), ("batch8", 8)):
+        if world == 1:
+            try:
+                out[key] = run_model_decode(layers, device, batch=batch)
+            except Exception as e:                  # reported on the line; the headline stands
+                out[key] = {"error": f"{type(e).__name__}: {e}"[:300]}
+        else:                                       # every rank takes the same collective steps
+            out[key] = run_model_decode(layers, device, dred, rank, world, batch)
+    if world == 1:
+        try:
+            dl = dense_layers(len(layers), device)
+            out["bf16_batch1"] = run_model_decode(dl, device, dense=True)
+            del dl
+            torch.cuda.empty_cache()
+            if "tokens_per_s" in out.get("batch1", {}):
+                r = out["batch1"]["tokens_per_s"] / out["bf16_batch1"]["tokens_per_s"]
+                out["speedup_vs_bf16"] = round(r, 3)
+                out["speedup_note"] = ("whole-token tokens/s of the OABF decoder over the same decoder on "
+                                       "uncompressed bf16 linears (cuBLAS), both one CUDA graph per token; "
+                                       "target 3x, weight-byte ceiling of the linears 2.55x")
+        except Exception as e:
+            out["bf16_batch1"] = {"error": f"{type(e).__name__}: {e}"[:300]}
+    if dred is not None:
+        torch.cuda.synchronize(device)
+        dred.close()
+    return out
+
+
+def run_decode_sweep(layers, device, ms=(4, 16), steps=20):
+    """The 48-layer linear step at M = 4 and 16 bf16 tokens (one CUDA graph per step, as the
+    headline), with per-kind rates from per-kind graphs."""
+    res = {}
+    for m in ms:
+        ms_step, kms, _ = time_linear_step(layers, m, device, 1, None, steps)
+        tot = sum(algorithmic_bytes(layers, m, kk) for kk in KINDS)
+        res[f"m{m}"] = {"ms_per_step": round(ms_step, 4), "gbs": round(tot / (ms_step * 1e-3) / 1e9, 1),
+                        "tokens_per_s_linears": round(m * 1000.0 / ms_step, 1),
+                        "layers_gbs": {kk: round(algorithmic_bytes(layers, m, kk) / (kms[kk] * 1e-3) / 1e9, 1)
+                                       for kk in KINDS}}
+    return res
+
+
+def dense_layers(n_layers, device):
+    """bf16 weights of the 12B-class layer shapes (random, N(0, 0.02)) for the uncompressed
+    baseline decoder: q|k|v, o, gate|up, down per layer."""
+    shapes = {"qkv": (8192, 3840), "o": (3840, 4096), "gate_up": (30720, 3840), "down": (3840, 15360)}
+    g = torch.Generator(device=device).manual_seed(77)
+    return [{kk: (0.02 * torch.randn(n, k, generator=g, device=device)).to(torch.bfloat16)
+             for kk, (n, k) in shapes.items()} for _ in range(n_layers)]
+
+
+LLAMA70B = dict(n_heads=64, n_kv_heads=8, head_dim=128, inter=28672, vocab=128256, hidden=8192)
+
+
+def time_linear_step(layers, m, device, world, reducer, steps):
+    """One decode step over `layers` (q|k|v, o, gate|up, down per layer in model order; the
+    row-parallel o and down summed over the ranks, fused into the GEMV where every shard takes
+    it) as one CUDA graph: (ms per step max over ranks, per-kind ms, kinds fused)."""
+    import torch.distributed as dist
+    from flashbfp_b200 import _lib
+    from flashbfp_b200.linear import fused_shard_eligible
+    L = _lib.lib()
+    fused = set()
+    if world > 1:
+        fused = {kk for kk in ("o", "down")
+                 if all(fused_shard_eligible(Ly[kk], reducer.max_elems) for Ly in layers)}
+        got = [None] * world
+        dist.all_gather_object(got, sorted(fused))
+        fused = set.intersection(*(set(g) for g in got))
+    rowpar = {"o", "down"} if world > 1 else set()
+    xs, outs = step_io(layers, m, device, rowpar - fused)
+    ws = {kk: torch.zeros(L.fbfp_gemv_workspace_bytes(16, layers[0][kk].npad), dtype=torch.uint8,
+                          device=device) for kk in KINDS}
+
+    def one(kk, li):
+        Ly = layers[li]
+        if kk in fused:
+            _gemv_fused(L, _lib, xs[kk], Ly[kk], outs[li][kk], ws[kk], reducer)
+        else:
+            _gemv(L, _lib, xs[kk], Ly[kk], outs[li][kk], ws[kk])
+            if kk in rowpar:
+                reducer(outs[li][kk])
+
+    st = torch.cuda.Stream(device)
+    st.wait_stream(torch.cuda.current_stream(device))
+    graphs = {}
+    with torch.cuda.stream(st):
+        for li in range(len(layers)):
+            for kk in KINDS:
+                one(kk, li)
+    torch.cuda.synchronize(device)
+    for kk in KINDS:
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=st):
+            for li in range(len(layers)):
+                one(kk, li)
+        graphs[kk] = g
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g, stream=st):
+        for li in range(len(layers)):
+            for kk in KINDS:
+                one(kk, li)
+    graphs["step"] = g
+    with torch.cuda.stream(st):
+        for _ in range(3):
+            g.replay()
+    torch.cuda.synchronize(device)
+    if world > 1:
+        dist.barrier()
+    ev = [torch.cuda.Event(enable_timing=True) for _ in range(6)]
+    kreps = max(1, steps // 4)
+    with torch.cuda.stream(st):
+        ev[0].record(st)
+        for _ in range(steps):
+            g.replay()
+        ev[1].record(st)
+        for i, kk in enumerate(KINDS):
+            for _ in range(kreps):
+                graphs[kk].replay()
+            ev[2 + i].record(st)
+    torch.cuda.synchronize(device)
+    for kk in KINDS:
+        _lib.check(L.fbfp_gemv_check(_lib.ptr(ws[kk]), _lib.stream_ptr(device)), "fbfp_gemv_check")
+    t = [ev[0].elapsed_time(ev[1]) / steps]
+    prev = ev[1]
+    for i in range(len(KINDS)):
+        t.append(prev.elapsed_time(ev[2 + i]) / kreps)
+        prev = ev[2 + i]
+    tt = torch.tensor(t, dtype=torch.float64, device=device)
+    if world > 1:
+        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+    for gg in graphs.values():
+        gg.reset()
+    return float(tt[0]), {kk: float(tt[1 + i]) for i, kk in enumerate(KINDS)}, fused
+
+
+def run_stress70b(device, rank, world, steps=10):
+    """70B-class stress (hidden 8192, 64 q / 8 kv heads of 128, MLP 28672): decode M=1 over 80
+    layers at 1.5% outliers, tensor-parallel over the ranks; at one GPU also the outlier
+    fractions 0.5 / 1.5 / 5% on 8 layers, the prefill GEMM at M = 4096 and the GPU compressor on
+    the gate|up matrix. Weights drawn on the GPU shard by shard, never whole on the host."""
+    import torch.distributed as dist
+    from flashbfp_b200 import OABFCompressor, workloads
+    from flashbfp_b200.linear import packed_linear, check_device_errors
+    out = {"shape": "hidden 8192, q 8192x8192, k/v 1024x8192, o 8192x8192, gate/up 28672x8192, "
+                    "down 8192x28672 per layer"}
+    reducer = None
+    if world > 1:
+        from flashbfp_b200.tp import NVLinkAllReduce
+        reducer = NVLinkAllReduce(16 * 8192)
+    layers, _ = build_layers(80, rank, world, device, workloads.LLAMA70B_LAYER, LLAMA70B, 0.015, 50000)
+    ms, kms, fused = time_linear_step(layers, 1, device, world, reducer, steps)
+    b = torch.tensor([algorithmic_bytes(layers, 1, kk) for kk in KINDS], dtype=torch.float64, device=device)
+    if world > 1:
+        dist.all_reduce(b)
+    tot = float(b.sum())
+    out["decode_m1_80_layers"] = {
+        "parallelism": f"tp{world}", "ms_per_step": round(ms, 4),
+        "gbs": round(tot / (ms * 1e-3) / 1e9, 1),
+        "frac_of_hbm_per_gpu": round(tot / world / (ms * 1e-3) / 1e9 / _peaks()["hbm_gbs"], 4),
+        "tokens_per_s_linears": round(1000.0 / ms, 1),
+        "layers_gbs_per_rank": {kk: round(float(b[i]) / world / (kms[kk] * 1e-3) / 1e9, 1)
+                                for i, kk in enumerate(KINDS)},
+        "exchange_fused": sorted(fused), "packed_gb_total": round(tot / 1e9, 2)}
+    if world == 1:
+        pf = []
+        for kk in ("gate_up", "down"):
+            pw = layers[0][kk]
+            X = workloads.activations(4096, pw.k_in, seed=3, device=device)
+            Y = torch.empty(4096, pw.n_out, dtype=torch.bfloat16, device=device)
+            for _ in range(2):
+                packed_linear(X, pw, out=Y)
+            torch.cuda.synchronize(device)
+            a, c = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record()
+            for _ in range(3):
+                packed_linear(X, pw, out=Y)
+            c.record()
+            torch.cuda.synchronize(device)
+            check_device_errors(device)
+            t = a.elapsed_time(c) / 3
+            tf = 2.0 * 4096 * pw.n_out * pw.k_in / (t * 1e-3) / 1e12
+            pf.append({"linear": f"{kk} {pw.n_out}x{pw.k_in}", "m": 4096, "ms": round(t, 3),
+                       "tflops": round(tf, 1), "frac": round(tf / _peaks()["bf16_tflops"], 4)})
+            del X, Y
+        out["prefill_m4096"] = pf
+        del layers
+        torch.cuda.empty_cache()
+        W = workloads.decode_weight(57344, 8192, seed=9, device=device)
+        comp = OABFCompressor()
+        for _ in range(2):
+            dp, sp = comp.compress_matrix_device(W)
+        torch.cuda.synchronize(device)
+        a, c = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        for _ in range(3):
+            dp, sp = comp.compress_matrix_device(W)
+        c.record()
+        torch.cuda.synchronize(device)
+        t = a.elapsed_time(c) / 3
+        out["compress_gate_up"] = {"matrix": "57344x8192 bf16", "ms": round(t, 3),
+                                   "input_gbs": round(2.0 * W.numel() / (t * 1e-3) / 1e9, 1),
+                                   "algorithmic_gbs": round((2.0 * W.numel() + 11.0 * dp["exponents"].numel()
+                                                             + 10.0 * int(sp["count"])) / (t * 1e-3) / 1e9, 1)}
+        del W, dp, sp
+        torch.cuda.empty_cache()
+        sweep = {}
+        for frac in (0.005, 0.015, 0.05):
+            ly, _ = build_layers(8, 0, 1, device, workloads.LLAMA70B_LAYER, LLAMA70B, frac, 60000)
+            ms8, kms8, _ = time_linear_step(ly, 1, device, 1, None, steps)
+            tot8 = sum(algorithmic_bytes(ly, 1, kk) for kk in KINDS)
+            sweep[f"{frac * 100:g}%"] = {"ms_per_step_8_layers": round(ms8, 4),
+                                         "gbs": round(tot8 / (ms8 * 1e-3) / 1e9, 1),
+                                         "outliers_per_layer": int(sum(ly[0][kk].nnz for kk in KINDS)),
+                                         "layers_gbs": {kk: round(algorithmic_bytes(ly, 1, kk) / (kms8[kk] * 1e-3) / 1e9, 1)
+                                                        for kk in KINDS}}
+            del ly
+            torch.cuda.empty_cache()
+        out["outlier_sweep_m1_8_layers"] = sweep
+    else:
+        del layers
+        torch.cuda.empty_cache()
+    if reducer is not None:
+        torch.cuda.synchronize(device)
+        reducer.close()
+    return out
 
 
 def run_bf16_decode(device, m=1, n_layers=8, iters=50):

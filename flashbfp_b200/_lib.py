@@ -58,6 +58,11 @@ _PROTOS = {
     "fbfp_decode_attention": (_c_int, [_vp, _c_i64, _vp, _vp, _c_i64, _c_i64, _c_i64, _c_i64, _vp, _c_i64,
                                        ctypes.c_float, _vp, _vp]),
     "fbfp_geglu": (_c_int, [_vp, _c_i64, _c_i64, _vp, _vp]),
+    "fbfp_decode_attention_step_scratch_bytes": (_c_i64, [_c_i64, _c_i64, _c_i64, _c_i64]),
+    "fbfp_decode_attention_step": (_c_int, [_vp, _c_i64, _c_i64, _c_i64, _c_i64, _vp, _vp, ctypes.c_float,
+                                            _vp, _vp, _vp, _c_i64, _vp, _vp, _c_i64, _c_i64, ctypes.c_float,
+                                            _vp, _vp, _vp, _vp]),
+    "fbfp_advance_positions": (_c_int, [_vp, _c_i64, _vp]),
     "fbfp_advance_position": (_c_int, [_vp, _c_i64, _vp]),
     "fbfp_allreduce_ipc_handle_bytes": (_c_i64, []),
     "fbfp_allreduce_create": (_c_int, [_c_int, _c_int, _c_i64, _vp, _vp]),

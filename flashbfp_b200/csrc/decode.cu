@@ -120,6 +120,126 @@ __global__ void rmsnorm_kernel(const bf16* x, const bf16* w, float eps, int hidd
     y[off + d] = __float2bfloat16_rn(sh[d] * r * (1.f + ldb(w + d)));
 }
 
+__device__ __forceinline__ void unpack8(const uint4& u, float (&f)[8]) {
+  const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    f[2 * i] = __uint_as_float(w[i] << 16);
+    f[2 * i + 1] = __uint_as_float(w[i] & 0xFFFF0000u);
+  }
+}
+
+// Vectorised forms of the two norm kernels for hidden a multiple of 8 and at most
+// 8 * kNormThreads * NV: every thread keeps its NV groups of 8 values in registers (one 16-byte
+// load each), so a row is read once and reduced once per RMSNorm (one shuffle tree, one barrier).
+__device__ __forceinline__ float row_sum_fast(float v, float* red) {
+  constexpr int nw = kNormThreads / 32;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  if (lane == 0) red[warp] = v;
+  __syncthreads();
+  float t = 0.f;
+#pragma unroll
+  for (int w = 0; w < nw; ++w) t += red[w];
+  return t;
+}
+
+__device__ __forceinline__ void load8(const bf16* p, float (&f)[8]) {
+  unpack8(*reinterpret_cast<const uint4*>(p), f);
+}
+
+__device__ __forceinline__ void store8(bf16* p, const float (&f)[8]) {
+  uint32_t w[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const uint32_t lo = __bfloat16_as_ushort(__float2bfloat16_rn(f[2 * i]));
+    const uint32_t hi = __bfloat16_as_ushort(__float2bfloat16_rn(f[2 * i + 1]));
+    w[i] = lo | (hi << 16);
+  }
+  *reinterpret_cast<uint4*>(p) = make_uint4(w[0], w[1], w[2], w[3]);
+}
+
+template <int NV>
+__global__ void __launch_bounds__(kNormThreads) rmsnorm_vec_kernel(const bf16* x, const bf16* w, float eps,
+                                                                    int hidden, bf16* y) {
+  pdl_prologue();
+  __shared__ float red[kNormThreads / 32];
+  const int64_t off = (int64_t)blockIdx.x * hidden;
+  float v[NV][8];
+  float ss = 0.f;
+#pragma unroll
+  for (int i = 0; i < NV; ++i) {
+    const int d = (threadIdx.x + i * kNormThreads) * 8;
+    if (d < hidden) {
+      load8(x + off + d, v[i]);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) ss += v[i][e] * v[i][e];
+    }
+  }
+  const float r = rsqrtf(row_sum_fast(ss, red) / (float)hidden + eps);
+#pragma unroll
+  for (int i = 0; i < NV; ++i) {
+    const int d = (threadIdx.x + i * kNormThreads) * 8;
+    if (d < hidden) {
+      float wv[8], o[8];
+      load8(w + d, wv);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) o[e] = v[i][e] * r * (1.f + wv[e]);
+      store8(y + off + d, o);
+    }
+  }
+}
+
+template <int NV>
+__global__ void __launch_bounds__(kNormThreads) post_residual_pre_vec_kernel(
+    const bf16* y, const bf16* w_post, bf16* resid, const bf16* w_pre, float eps, int hidden, bf16* x_next) {
+  pdl_prologue();
+  __shared__ float red[2][kNormThreads / 32];
+  const int64_t off = (int64_t)blockIdx.x * hidden;
+  float v[NV][8];
+  float ss = 0.f;
+#pragma unroll
+  for (int i = 0; i < NV; ++i) {
+    const int d = (threadIdx.x + i * kNormThreads) * 8;
+    if (d < hidden) {
+      load8(y + off + d, v[i]);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) ss += v[i][e] * v[i][e];
+    }
+  }
+  const float r1 = rsqrtf(row_sum_fast(ss, red[0]) / (float)hidden + eps);
+  float hs = 0.f;
+#pragma unroll
+  for (int i = 0; i < NV; ++i) {
+    const int d = (threadIdx.x + i * kNormThreads) * 8;
+    if (d < hidden) {
+      float wv[8], rv[8];
+      load8(w_post + d, wv);
+      load8(resid + off + d, rv);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        const float h = bfr(rv[e] + bfr(v[i][e] * r1 * (1.f + wv[e])));
+        v[i][e] = h;
+        hs += h * h;
+      }
+      store8(resid + off + d, v[i]);
+    }
+  }
+  const float r2 = rsqrtf(row_sum_fast(hs, red[1]) / (float)hidden + eps);
+#pragma unroll
+  for (int i = 0; i < NV; ++i) {
+    const int d = (threadIdx.x + i * kNormThreads) * 8;
+    if (d < hidden) {
+      float wv[8], o[8];
+      load8(w_pre + d, wv);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) o[e] = v[i][e] * r2 * (1.f + wv[e]);
+      store8(x_next + off + d, o);
+    }
+  }
+}
+
 // Between a layer's halves, per row: h = bf16(resid + post_norm(y)); resid = h;
 // x_next = pre_norm(h). One CTA per row.
 __global__ void post_residual_pre_kernel(const bf16* y, const bf16* w_post, bf16* resid,
@@ -200,15 +320,6 @@ __global__ void qk_rope_cache_kernel(const bf16* qkv, int nh, int nkv, int hd, c
 // 16-byte load of a cache row; head_dim <= 256, a multiple of 8); warp w takes the positions
 // j = w (mod warps) for both the scores and the weighted sum, whose per-warp partial rows are
 // added in shared memory at the end.
-__device__ __forceinline__ void unpack8(const uint4& u, float (&f)[8]) {
-  const uint32_t w[4] = {u.x, u.y, u.z, u.w};
-#pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    f[2 * i] = __uint_as_float(w[i] << 16);
-    f[2 * i + 1] = __uint_as_float(w[i] & 0xFFFF0000u);
-  }
-}
-
 constexpr int kAttnThreads = 256;
 
 __global__ void __launch_bounds__(kAttnThreads)
@@ -278,6 +389,204 @@ decode_attention_kernel(const bf16* q, const bf16* kc, const bf16* vc, int nh, i
   }
 }
 
+// Decode attention for one new token per sequence (row r = sequence r of a batch, at its own
+// position pos[r], with its own caches at seq_stride elements from the previous sequence's), with
+// the q/k RMSNorm, the rotary embedding and the KV-cache append of fbfp_qk_rope_cache folded in,
+// and split over positions: CTA (head, row, split) covers the cached positions
+// [split * kFaChunk, (split + 1) * kFaChunk) of the row's window [lo, p]. It loads its cached
+// keys and values first (the loads overlap the norms), normalises and rotates its query head;
+// the CTAs whose range holds p compute the new key and value (the first query head of each KV
+// group also writes them to the cache) and use them from shared memory. Each CTA writes its
+// softmax partial (max, sum, weighted values) to scratch; the last of a (head, row)'s CTAs to
+// finish (an atomic count) merges them and returns the counter to zero for the next launch.
+// Same arithmetic as the two separate kernels (bf16 roundings of the norm and the rotation, fp32
+// scores and softmax), up to the order of the fp32 sums.
+constexpr int kFaThreads = 256;
+constexpr int kFaChunk = 64;
+
+// Normalise (RMSNorm over hd with weights 1 + w) and rotate one head of a fused q|k|v row into
+// dst (fp32 values that are bf16-rounded as the separate kernel rounds them). Every thread of
+// the CTA calls it; uses red (33 floats) and tmp (hd floats).
+__device__ void fa_norm_rope(const bf16* x, const bf16* w, float eps, int hd, const bf16* cr, const bf16* sr,
+                             float* tmp, float* red, float* dst) {
+  float ss = 0.f;
+  for (int d = threadIdx.x; d < hd; d += blockDim.x) {
+    const float v = ldb(x + d);
+    tmp[d] = v;
+    ss += v * v;
+  }
+  const float r = rsqrtf(block_sum(ss, red) / (float)hd + eps);
+  for (int d = threadIdx.x; d < hd; d += blockDim.x) tmp[d] = bfr(tmp[d] * r * (1.f + ldb(w + d)));
+  __syncthreads();
+  const int half = hd / 2;
+  for (int d = threadIdx.x; d < hd; d += blockDim.x) {
+    const float rot = d < half ? -tmp[d + half] : tmp[d - half];
+    dst[d] = bfr(bfr(tmp[d] * ldb(cr + d)) + bfr(rot * ldb(sr + d)));
+  }
+  __syncthreads();
+}
+
+__global__ void __launch_bounds__(kFaThreads)
+decode_attention_step_kernel(const bf16* qkv, int nh, int nkv, int hd, const bf16* qnw, const bf16* knw,
+                             float eps, const bf16* cos_t, const bf16* sin_t, const int32_t* pos, int max_ctx,
+                             bf16* kc, bf16* vc, int64_t seq_stride, int window, float scaling, int n_splits,
+                             float* part, int* counters, bf16* out, int32_t* err) {
+  pdl_prologue();
+  constexpr int nw = kFaThreads / 32;
+  constexpr int per_warp = kFaChunk / nw;
+  extern __shared__ float sh[];      // q, k_new, v_new, tmp (hd each), scores (kFaChunk), po (nw x hd), 33
+  float* qf = sh;
+  float* kn = qf + hd;
+  float* vn = kn + hd;
+  float* tmp = vn + hd;
+  float* sc = tmp + hd;
+  float* po = sc + kFaChunk;
+  float* red = po + nw * hd;
+  __shared__ int s_last;
+  const int head = blockIdx.x, row = blockIdx.y, split = blockIdx.z, rows = gridDim.y;
+  const int group = nh / nkv, kvh = head / group;
+  const int p = pos[row];
+  if (p < 0 || p >= max_ctx) {                   // the whole row is skipped (no CTA counts)
+    if (threadIdx.x == 0 && head == 0 && split == 0) atomicExch(err, 2);
+    return;
+  }
+  const int lo = (window > 0 && p - window + 1 > 0) ? p - window + 1 : 0;
+  const int c0 = max(lo, split * kFaChunk), c1 = min(p + 1, (split + 1) * kFaChunk);
+  float* mine = part + (((int64_t)head * rows + row) * n_splits + split) * (hd + 2);
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  if (c0 < c1) {
+    const bf16* xrow = qkv + (int64_t)row * (nh + 2 * nkv) * hd;
+    const bf16* cr = cos_t + (int64_t)p * hd;
+    const bf16* sr = sin_t + (int64_t)p * hd;
+    bf16* kbase = kc + row * seq_stride + (int64_t)kvh * max_ctx * hd;
+    bf16* vbase = vc + row * seq_stride + (int64_t)kvh * max_ctx * hd;
+    const bool act = lane * 8 < hd;
+    // the cached keys and values of this range first: their loads overlap the norms below
+    // (warp w takes positions c0 + w + nw * i)
+    uint4 kr[per_warp], vr[per_warp];
+#pragma unroll
+    for (int i = 0; i < per_warp; ++i) {
+      const int j = c0 + warp + nw * i;
+      const bool ld = act && j < c1 && j != p;
+      kr[i] = ld ? *reinterpret_cast<const uint4*>(kbase + (int64_t)j * hd + lane * 8) : make_uint4(0, 0, 0, 0);
+      vr[i] = ld ? *reinterpret_cast<const uint4*>(vbase + (int64_t)j * hd + lane * 8) : make_uint4(0, 0, 0, 0);
+    }
+    fa_norm_rope(xrow + (int64_t)head * hd, qnw, eps, hd, cr, sr, tmp, red, qf);
+    const bool has_new = c1 == p + 1;
+    if (has_new) {
+      fa_norm_rope(xrow + (int64_t)(nh + kvh) * hd, knw, eps, hd, cr, sr, tmp, red, kn);
+      const bf16* vsrc = xrow + (int64_t)(nh + nkv + kvh) * hd;
+      for (int d = threadIdx.x; d < hd; d += blockDim.x) vn[d] = ldb(vsrc + d);
+      if (head % group == 0) {
+        for (int d = threadIdx.x; d < hd; d += blockDim.x) {
+          kbase[(int64_t)p * hd + d] = __float2bfloat16_rn(kn[d]);
+          vbase[(int64_t)p * hd + d] = vsrc[d];
+        }
+      }
+      __syncthreads();
+    }
+    float q8[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) q8[i] = act ? qf[lane * 8 + i] : 0.f;
+#pragma unroll
+    for (int i = 0; i < per_warp; ++i) {
+      const int j = c0 + warp + nw * i;
+      float kv[8];
+      if (j == p) {
+#pragma unroll
+        for (int e = 0; e < 8; ++e) kv[e] = act ? kn[lane * 8 + e] : 0.f;
+      } else {
+        unpack8(kr[i], kv);
+      }
+      float acc = 0.f;
+#pragma unroll
+      for (int e = 0; e < 8; ++e) acc += q8[e] * kv[e];
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+      if (lane == 0 && j < c1) sc[j - c0] = acc * scaling;
+    }
+    __syncthreads();
+    const int n = c1 - c0;
+    float m = -INFINITY;
+    for (int j = threadIdx.x; j < n; j += blockDim.x) m = fmaxf(m, sc[j]);
+    m = block_max(m, red);
+    float ssum = 0.f;
+    for (int j = threadIdx.x; j < n; j += blockDim.x) {
+      const float e = __expf(sc[j] - m);
+      sc[j] = e;
+      ssum += e;
+    }
+    const float l = block_sum(ssum, red);        // ends with a barrier: every sc[j] is final
+    float o8[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+    if (act) {
+#pragma unroll
+      for (int i = 0; i < per_warp; ++i) {
+        const int j = c0 + warp + nw * i;
+        if (j >= c1) continue;
+        float vv[8];
+        if (j == p) {
+#pragma unroll
+          for (int e = 0; e < 8; ++e) vv[e] = vn[lane * 8 + e];
+        } else {
+          unpack8(vr[i], vv);
+        }
+        const float pj = sc[j - c0];
+#pragma unroll
+        for (int e = 0; e < 8; ++e) o8[e] += pj * vv[e];
+      }
+#pragma unroll
+      for (int e = 0; e < 8; ++e) po[warp * hd + lane * 8 + e] = o8[e];
+    }
+    __syncthreads();
+    for (int d = threadIdx.x; d < hd; d += blockDim.x) {
+      float acc = 0.f;
+#pragma unroll
+      for (int w = 0; w < nw; ++w) acc += po[w * hd + d];
+      mine[2 + d] = acc;
+    }
+    if (threadIdx.x == 0) { mine[0] = m; mine[1] = l; }
+  } else if (threadIdx.x == 0) {                 // no position of the window in this range
+    mine[0] = -INFINITY;
+    mine[1] = 0.f;
+  }
+  // the last CTA of (head, row) merges the partials
+  __threadfence();
+  __syncthreads();
+  if (threadIdx.x == 0) s_last = atomicAdd(counters + head * rows + row, 1) == n_splits - 1;
+  __syncthreads();
+  if (!s_last) return;
+  __threadfence();
+  const float* base = part + ((int64_t)head * rows + row) * n_splits * (hd + 2);
+  float M = -INFINITY;
+  for (int s2 = 0; s2 < n_splits; ++s2) {
+    const float* ps = base + (int64_t)s2 * (hd + 2);
+    if (__ldcg(ps + 1) > 0.f) M = fmaxf(M, __ldcg(ps));
+  }
+  float L = 0.f;
+  for (int s2 = 0; s2 < n_splits; ++s2) {
+    const float* ps = base + (int64_t)s2 * (hd + 2);
+    const float ls = __ldcg(ps + 1);
+    if (ls > 0.f) L += ls * __expf(__ldcg(ps) - M);
+  }
+  const float inv = 1.f / L;
+  bf16* orow = out + ((int64_t)row * nh + head) * hd;
+  for (int d = threadIdx.x; d < hd; d += blockDim.x) {
+    float acc = 0.f;
+    for (int s2 = 0; s2 < n_splits; ++s2) {
+      const float* ps = base + (int64_t)s2 * (hd + 2);
+      const float ls = __ldcg(ps + 1);
+      if (ls > 0.f) acc += __ldcg(ps + 2 + d) * __expf(__ldcg(ps) - M);
+    }
+    orow[d] = __float2bfloat16_rn(acc * inv);
+  }
+  if (threadIdx.x == 0) counters[head * rows + row] = 0;
+}
+
+__global__ void advance_rows_kernel(int32_t* pos, int b) {
+  pdl_prologue();
+  if ((int)threadIdx.x < b) pos[threadIdx.x] += 1;
+}
+
 // out[r][i] = bf16(bf16(gelu_tanh(gate[r][i])) * up[r][i]) for the fused rows [gate (I) | up (I)].
 __global__ void geglu_kernel(const bf16* gu, int64_t inter, int64_t total, bf16* out) {
   pdl_prologue();
@@ -316,6 +625,15 @@ extern "C" int fbfp_rmsnorm(const void* x, int64_t m, const void* w, float eps, 
                             void* stream) {
   FBFP_CHECK_ARG(x && w && y && hidden > 0 && hidden <= 12000, "bad arguments (hidden <= 12000)");
   FBFP_CHECK_ARG(m >= 1 && m <= 65535, "m must be in [1, 65535]");
+  const int nv = (int)((hidden + 8 * kNormThreads - 1) / (8 * kNormThreads));
+  if (hidden % 8 == 0 && nv <= 3 && ((uintptr_t)x & 15) == 0 && ((uintptr_t)w & 15) == 0 && ((uintptr_t)y & 15) == 0) {
+    auto k = nv == 1 ? rmsnorm_vec_kernel<1> : nv == 2 ? rmsnorm_vec_kernel<2> : rmsnorm_vec_kernel<3>;
+    FBFP_CUDA_TRY(launch_pdl(k, dim3((unsigned)m), dim3(kNormThreads), 0, as_stream(stream),
+                             reinterpret_cast<const bf16*>(x), reinterpret_cast<const bf16*>(w), eps, (int)hidden,
+                             reinterpret_cast<bf16*>(y)));
+    FBFP_LAUNCH_CHECK("rmsnorm_vec_kernel");
+    return FBFP_OK;
+  }
   const size_t smem = sizeof(float) * ((size_t)hidden + 33);
   FBFP_CUDA_TRY(launch_pdl(rmsnorm_kernel, dim3((unsigned)m), dim3(kNormThreads), smem, as_stream(stream),
                            reinterpret_cast<const bf16*>(x), reinterpret_cast<const bf16*>(w), eps, (int)hidden,
@@ -330,6 +648,18 @@ extern "C" int fbfp_post_residual_norm(const void* y, int64_t m, const void* w_p
   FBFP_CHECK_ARG(y && w_post && resid && w_pre && x_next && hidden > 0 && hidden <= 12000,
                  "bad arguments (hidden <= 12000)");
   FBFP_CHECK_ARG(m >= 1 && m <= 65535, "m must be in [1, 65535]");
+  const int nv = (int)((hidden + 8 * kNormThreads - 1) / (8 * kNormThreads));
+  if (hidden % 8 == 0 && nv <= 3 && ((uintptr_t)y & 15) == 0 && ((uintptr_t)w_post & 15) == 0 &&
+      ((uintptr_t)resid & 15) == 0 && ((uintptr_t)w_pre & 15) == 0 && ((uintptr_t)x_next & 15) == 0) {
+    auto k = nv == 1 ? post_residual_pre_vec_kernel<1>
+                     : nv == 2 ? post_residual_pre_vec_kernel<2> : post_residual_pre_vec_kernel<3>;
+    FBFP_CUDA_TRY(launch_pdl(k, dim3((unsigned)m), dim3(kNormThreads), 0, as_stream(stream),
+                             reinterpret_cast<const bf16*>(y), reinterpret_cast<const bf16*>(w_post),
+                             reinterpret_cast<bf16*>(resid), reinterpret_cast<const bf16*>(w_pre), eps, (int)hidden,
+                             reinterpret_cast<bf16*>(x_next)));
+    FBFP_LAUNCH_CHECK("post_residual_pre_vec_kernel");
+    return FBFP_OK;
+  }
   const size_t smem = sizeof(float) * ((size_t)hidden + 33);
   FBFP_CUDA_TRY(launch_pdl(post_residual_pre_kernel, dim3((unsigned)m), dim3(kNormThreads), smem,
                            as_stream(stream), reinterpret_cast<const bf16*>(y),
@@ -395,5 +725,55 @@ extern "C" int fbfp_advance_position(int32_t* pos, int64_t m, void* stream) {
   FBFP_CHECK_ARG(pos && m >= 1 && m <= 65535, "bad arguments");
   FBFP_CUDA_TRY(launch_pdl(advance_kernel, dim3(1), dim3(1), 0, as_stream(stream), pos, (int)m));
   FBFP_LAUNCH_CHECK("advance_kernel");
+  return FBFP_OK;
+}
+
+extern "C" int64_t fbfp_decode_attention_step_scratch_bytes(int64_t b, int64_t nh, int64_t hd, int64_t max_ctx) {
+  if (b < 1 || nh < 1 || hd < 1 || max_ctx < 1) return -1;
+  const int64_t splits = (max_ctx + kFaChunk - 1) / kFaChunk;
+  const int64_t counters = (nh * b * 4 + 255) / 256 * 256;
+  return counters + nh * b * splits * (hd + 2) * 4;
+}
+
+extern "C" int fbfp_decode_attention_step(const void* qkv, int64_t b, int64_t nh, int64_t nkv, int64_t hd,
+                                          const void* q_norm_w, const void* k_norm_w, float eps,
+                                          const void* cos_table, const void* sin_table, const int32_t* pos,
+                                          int64_t max_ctx, void* k_cache, void* v_cache, int64_t seq_stride,
+                                          int64_t window, float scaling, void* scratch, void* out, int32_t* err,
+                                          void* stream) {
+  FBFP_CHECK_ARG(qkv && q_norm_w && k_norm_w && cos_table && sin_table && pos && k_cache && v_cache && scratch &&
+                     out && err,
+                 "null pointer");
+  FBFP_CHECK_ARG(nh > 0 && nkv > 0 && nh % nkv == 0 && hd > 0 && hd <= 256 && hd % 8 == 0,
+                 "bad head shape (nh %lld, nkv %lld, hd %lld: hd a multiple of 8 up to 256)", (long long)nh,
+                 (long long)nkv, (long long)hd);
+  FBFP_CHECK_ARG(b >= 1 && b <= 65535 && max_ctx > 0 && max_ctx < (1 << 30), "bad batch %lld or max_ctx %lld",
+                 (long long)b, (long long)max_ctx);
+  FBFP_CHECK_ARG(b == 1 || seq_stride >= nkv * max_ctx * hd, "seq_stride %lld below one sequence's cache",
+                 (long long)seq_stride);
+  FBFP_CHECK_ARG(((uintptr_t)k_cache & 15) == 0 && ((uintptr_t)v_cache & 15) == 0 && (seq_stride % 8) == 0,
+                 "caches must be 16-byte aligned (seq_stride a multiple of 8)");
+  FBFP_CHECK_ARG(((uintptr_t)scratch & 15) == 0, "scratch must be 16-byte aligned");
+  const int64_t splits = (max_ctx + kFaChunk - 1) / kFaChunk;
+  FBFP_CHECK_ARG(splits <= 65535, "max_ctx too large");
+  int* counters = reinterpret_cast<int*>(scratch);
+  float* part = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(scratch) + (nh * b * 4 + 255) / 256 * 256);
+  const size_t smem = sizeof(float) * (4 * (size_t)hd + kFaChunk + (kFaThreads / 32) * (size_t)hd + 33);
+  FBFP_CUDA_TRY(launch_pdl(decode_attention_step_kernel, dim3((unsigned)nh, (unsigned)b, (unsigned)splits),
+                           dim3(kFaThreads), smem, as_stream(stream), reinterpret_cast<const bf16*>(qkv), (int)nh,
+                           (int)nkv, (int)hd, reinterpret_cast<const bf16*>(q_norm_w),
+                           reinterpret_cast<const bf16*>(k_norm_w), eps, reinterpret_cast<const bf16*>(cos_table),
+                           reinterpret_cast<const bf16*>(sin_table), pos, (int)max_ctx,
+                           reinterpret_cast<bf16*>(k_cache), reinterpret_cast<bf16*>(v_cache), seq_stride,
+                           (int)window, scaling, (int)splits, part, counters, reinterpret_cast<bf16*>(out), err));
+  FBFP_LAUNCH_CHECK("decode_attention_step_kernel");
+  return FBFP_OK;
+}
+
+extern "C" int fbfp_advance_positions(int32_t* pos, int64_t b, void* stream) {
+  FBFP_CHECK_ARG(pos && b >= 1 && b <= 1024, "bad arguments (1 <= b <= 1024)");
+  FBFP_CUDA_TRY(launch_pdl(advance_rows_kernel, dim3(1), dim3((unsigned)((b + 31) / 32 * 32)), 0,
+                           as_stream(stream), pos, (int)b));
+  FBFP_LAUNCH_CHECK("advance_rows_kernel");
   return FBFP_OK;
 }

@@ -91,7 +91,7 @@ class GemmaDecoder:
 
     def __init__(self, shape: DecoderShape, layers: List[DecodeLayer], embed: torch.Tensor,
                  final_norm: torch.Tensor, lm_head: torch.Tensor, max_ctx: int, device=None,
-                 max_prefill: int = 128, reducer=None, vocab_offset: int = 0):
+                 max_prefill: int = 128, reducer=None, vocab_offset: int = 0, batch: int = 1):
         self.L = _lib.lib()
         self.shape, self.layers = shape, layers
         dev = torch.device(device) if device is not None else embed.device
@@ -134,10 +134,15 @@ class GemmaDecoder:
             "sliding_attention": rope_tables(s.rope_theta_local, s.head_dim, self.max_ctx, dev),
             "full_attention": rope_tables(s.rope_theta_global, s.head_dim, self.max_ctx, dev),
         }
-        cache = (len(layers), self.hkv, self.max_ctx, s.head_dim)
+        B = self.batch = int(batch)
+        if not 1 <= B <= 64:
+            raise ValueError(f"batch {B} outside [1, 64]")
+        cache = (len(layers), B, self.hkv, self.max_ctx, s.head_dim)      # per layer and sequence
         self.k_cache = torch.zeros(cache, **bf)
         self.v_cache = torch.zeros(cache, **bf)
-        R = self.max_rows = max(1, int(max_prefill))         # rows of a prompt chunk
+        self.seq_stride = self.hkv * self.max_ctx * s.head_dim
+        self.max_rows = max(1, int(max_prefill))             # rows of a prompt chunk
+        R = max(self.max_rows, B)
         self.h = torch.zeros(R, s.hidden, **bf)              # residual stream
         self.x = torch.zeros(R, s.hidden, **bf)              # normalised input of the next linear
         self.qkv = torch.zeros(R, q_rows, **bf)
@@ -147,18 +152,22 @@ class GemmaDecoder:
         self.gu = torch.zeros(R, 2 * self.inter_l, **bf)
         self.act = torch.zeros(R, self.inter_l, **bf)
         self.down = torch.zeros(R, s.hidden, **bf)
-        self.logits = torch.zeros(1, self.vocab_l, **bf)     # this rank's vocabulary rows
+        self.logits = torch.zeros(B, self.vocab_l, **bf)     # per sequence: this rank's vocabulary rows
         if reducer is not None:
             from .linear import fused_shard_eligible
-            if reducer.max_elems < max(R * s.hidden, 2 * self.world):
+            if reducer.max_elems < max(R * s.hidden, 2 * self.world * B):
                 raise ValueError(f"the reducer holds {reducer.max_elems} values; a prompt chunk of "
                                  f"{R} rows needs {R * s.hidden}")
             self.fused_rows = all(fused_shard_eligible(pw, reducer.max_elems)
                                   for ly in layers for pw in (ly.o, ly.down))
-            self.pick = torch.zeros(2 * self.world, dtype=torch.float32, device=dev)
+            self.pick = torch.zeros(B, 2 * self.world, dtype=torch.float32, device=dev)
             self.row_f32 = torch.zeros(R, s.hidden, dtype=torch.float32, device=dev)
-        self.tok = torch.zeros(R, dtype=torch.int64, device=dev)   # ids in; tok[0] = next token
-        self.pos = torch.zeros(1, dtype=torch.int32, device=dev)
+        self.ids = torch.zeros(R, dtype=torch.int64, device=dev)    # a prompt chunk's ids
+        self.tok = torch.zeros(B, dtype=torch.int64, device=dev)    # per sequence: current / next token
+        self.pos = torch.zeros(B, dtype=torch.int32, device=dev)    # per sequence: its position
+        self.attn_scratch = torch.zeros(
+            self.L.fbfp_decode_attention_step_scratch_bytes(B, self.hq, s.head_dim, self.max_ctx),
+            dtype=torch.uint8, device=dev)
         self.err = torch.zeros(1, dtype=torch.int32, device=dev)
         self.graph: Optional[torch.cuda.CUDAGraph] = None
         self.stream = torch.cuda.Stream(dev)
@@ -166,7 +175,7 @@ class GemmaDecoder:
     # -- construction from a Hugging Face Gemma-3 model after compress_gemma_model -----------
     @classmethod
     def from_hf(cls, model, max_ctx: int, device=None, max_prefill: int = 128,
-                reducer=None) -> "GemmaDecoder":
+                reducer=None, batch: int = 1) -> "GemmaDecoder":
         """The decoder of a Gemma-3 causal LM after ``compress_gemma_model``; with ``reducer``,
         of a model compressed with ``compress_gemma_model(..., rank=r, world=reducer.world)``
         on every rank (this rank's shards; lm_head rows split here)."""
@@ -219,7 +228,7 @@ class GemmaDecoder:
         elif any(hasattr(m, "tp_mode") for m in model.modules()):
             raise ValueError("the model holds tensor-parallel shards: pass the reducer")
         return cls(shape, layers, inner.embed_tokens.weight.data, inner.norm.weight.data,
-                   lm_head, max_ctx, dev, max_prefill, reducer=reducer, vocab_offset=v0)
+                   lm_head, max_ctx, dev, max_prefill, reducer=reducer, vocab_offset=v0, batch=batch)
 
     # -- one token ---------------------------------------------------------------------------
     def _linear(self, x: torch.Tensor, pw, out: torch.Tensor) -> None:
@@ -243,43 +252,48 @@ class GemmaDecoder:
             self.reducer(y)
             out.copy_(y)
 
-    def _pick(self, m: int) -> None:
-        """Greedy token of the last row's logits into self.tok[0]: argmax over this rank's
-        vocabulary rows, then (several ranks) every rank's (max, index) gathered through the
-        reducer (a sum of one-hot slots is exact) and the first maximum taken."""
+    def _pick(self, logits: torch.Tensor, tok: torch.Tensor, slots) -> None:
+        """Greedy tokens of `logits` rows into `tok`: argmax over this rank's vocabulary rows,
+        then (several ranks) every rank's (max, index) gathered through the reducer (a sum of
+        one-hot slots is exact) and the first maximum taken."""
         if self.reducer is None:
-            self.tok[:1].copy_(torch.argmax(self.logits, dim=-1))
+            tok.copy_(torch.argmax(logits, dim=-1))
             return
         from .tp import argmax_pick, argmax_slots
-        self.pick.zero_()
-        argmax_slots(self.logits, self.vocab_offset, self.rank, self.world, self.pick)
-        self.reducer(self.pick)
-        self.tok[:1].copy_(argmax_pick(self.pick))
+        slots.zero_()
+        argmax_slots(logits, self.vocab_offset, self.rank, self.world, slots)
+        self.reducer(slots)
+        tok.copy_(argmax_pick(slots, self.world))
 
-    def _enqueue(self, m: int) -> None:
-        """Rows 0..m-1 (tokens self.tok[:m] at positions self.pos ..): every layer, then the
-        logits of the last row, the greedy pick into self.tok[0] and pos += m."""
+    def _layers(self, m: int, chunk_seq: Optional[int]) -> None:
+        """Every layer over rows 0..m-1 of the activation buffers: with chunk_seq = b, a prompt
+        chunk of sequence b at positions pos[b] .. pos[b] + m - 1 (causal over the chunk);
+        with chunk_seq = None, one new token per sequence (m = batch)."""
         L, s, st = self.L, self.shape, _lib.stream_ptr(self.device)
         P = _lib.ptr
         eps = float(s.rms_norm_eps)
         h, x, qkv, q, attn = self.h[:m], self.x[:m], self.qkv[:m], self.q[:m], self.attn[:m]
         o, gu, act, down = self.o[:m], self.gu[:m], self.act[:m], self.down[:m]
-        _lib.check(L.fbfp_embed(P(self.tok), m, P(self.embed), s.vocab, s.hidden, self.embed_scale, P(h),
-                                P(self.err), st), "fbfp_embed")
-        _lib.check(L.fbfp_rmsnorm(P(h), m, P(self.layers[0].input_ln), eps, s.hidden, P(x), st),
-                   "fbfp_rmsnorm")
         for li, ly in enumerate(self.layers):
             kind = s.layer_types[li]
             cos_t, sin_t = self.rope[kind]
             window = s.sliding_window if kind == "sliding_attention" else 0
             self._linear(x, ly.qkv, qkv)
-            _lib.check(L.fbfp_qk_rope_cache(P(qkv), m, self.hq, self.hkv, s.head_dim, P(ly.q_norm),
-                                            P(ly.k_norm), eps, P(cos_t), P(sin_t), P(self.pos), self.max_ctx,
-                                            P(q), P(self.k_cache[li]), P(self.v_cache[li]), P(self.err), st),
-                       "fbfp_qk_rope_cache")
-            _lib.check(L.fbfp_decode_attention(P(q), m, P(self.k_cache[li]), P(self.v_cache[li]), self.hq,
-                                               self.hkv, s.head_dim, self.max_ctx, P(self.pos), window,
-                                               self.scaling, P(attn), st), "fbfp_decode_attention")
+            if chunk_seq is None:
+                _lib.check(L.fbfp_decode_attention_step(
+                    P(qkv), m, self.hq, self.hkv, s.head_dim, P(ly.q_norm), P(ly.k_norm), eps, P(cos_t),
+                    P(sin_t), P(self.pos), self.max_ctx, P(self.k_cache[li]), P(self.v_cache[li]),
+                    self.seq_stride, window, self.scaling, P(self.attn_scratch), P(attn), P(self.err), st),
+                    "fbfp_decode_attention_step")
+            else:
+                b = chunk_seq
+                kc, vc, pos = self.k_cache[li, b], self.v_cache[li, b], self.pos[b:b + 1]
+                _lib.check(L.fbfp_qk_rope_cache(P(qkv), m, self.hq, self.hkv, s.head_dim, P(ly.q_norm),
+                                                P(ly.k_norm), eps, P(cos_t), P(sin_t), P(pos), self.max_ctx,
+                                                P(q), P(kc), P(vc), P(self.err), st), "fbfp_qk_rope_cache")
+                _lib.check(L.fbfp_decode_attention(P(q), m, P(kc), P(vc), self.hq, self.hkv, s.head_dim,
+                                                   self.max_ctx, P(pos), window, self.scaling, P(attn), st),
+                           "fbfp_decode_attention")
             self._row_linear(attn, ly.o, o)
             _lib.check(L.fbfp_post_residual_norm(P(o), m, P(ly.post_attn_ln), P(h), P(ly.pre_ffn_ln), eps,
                                                  s.hidden, P(x), st), "fbfp_post_residual_norm")
@@ -289,33 +303,63 @@ class GemmaDecoder:
             nxt = self.layers[li + 1].input_ln if li + 1 < len(self.layers) else self.final_norm
             _lib.check(L.fbfp_post_residual_norm(P(down), m, P(ly.post_ffn_ln), P(h), P(nxt), eps,
                                                  s.hidden, P(x), st), "fbfp_post_residual_norm")
-        torch.matmul(x[m - 1:m], self.lm_head.t(), out=self.logits)     # bf16 lm_head (cuBLAS)
-        self._pick(m)
-        _lib.check(L.fbfp_advance_position(P(self.pos), m, st), "fbfp_advance_position")
+
+    def _embed(self, ids: torch.Tensor, m: int) -> None:
+        L, s, st = self.L, self.shape, _lib.stream_ptr(self.device)
+        P = _lib.ptr
+        _lib.check(L.fbfp_embed(P(ids), m, P(self.embed), s.vocab, s.hidden, self.embed_scale, P(self.h),
+                                P(self.err), st), "fbfp_embed")
+        _lib.check(L.fbfp_rmsnorm(P(self.h), m, P(self.layers[0].input_ln), float(s.rms_norm_eps), s.hidden,
+                                  P(self.x), st), "fbfp_rmsnorm")
+
+    def _enqueue(self, m: int, seq: int = 0) -> None:
+        """A prompt chunk of m tokens (self.ids[:m]) of sequence seq: every layer, then the logits
+        of the last row into self.logits[seq], the greedy pick into self.tok[seq] and pos[seq] += m."""
+        self._embed(self.ids, m)
+        self._layers(m, seq)
+        torch.matmul(self.x[m - 1:m], self.lm_head.t(), out=self.logits[seq:seq + 1])   # bf16 lm_head
+        self._pick(self.logits[seq:seq + 1], self.tok[seq:seq + 1],
+                   self.pick[seq:seq + 1] if self.reducer is not None else None)
+        _lib.check(self.L.fbfp_advance_position(_lib.ptr(self.pos[seq:seq + 1]), m, _lib.stream_ptr(self.device)),
+                   "fbfp_advance_position")
 
     def _enqueue_step(self) -> None:
-        self._enqueue(1)
+        """One new token for every sequence: tokens self.tok at positions self.pos; leaves the
+        logits in self.logits, the greedy next tokens in self.tok and advances every position."""
+        B = self.batch
+        self._embed(self.tok, B)
+        self._layers(B, None)
+        torch.matmul(self.x[:B], self.lm_head.t(), out=self.logits)          # bf16 lm_head (cuBLAS)
+        self._pick(self.logits, self.tok, self.pick if self.reducer is not None else None)
+        _lib.check(self.L.fbfp_advance_positions(_lib.ptr(self.pos), B, _lib.stream_ptr(self.device)),
+                   "fbfp_advance_positions")
 
-    def prefill(self, ids: Sequence[int]) -> None:
-        """Run a prompt chunk at positions self.pos .. (at most max_prefill tokens): fills the KV
-        cache, leaves the last row's logits in self.logits, the greedy next token in self.tok[0],
-        and advances self.pos by len(ids)."""
+    def prefill(self, ids: Sequence[int], seq: int = 0) -> None:
+        """Run a prompt chunk of sequence ``seq`` at positions pos[seq] .. (at most max_prefill
+        tokens): fills its KV cache, leaves the last row's logits in self.logits[seq], the greedy
+        next token in self.tok[seq], and advances pos[seq] by len(ids)."""
         m = len(ids)
         if not 1 <= m <= self.max_rows:
             raise ValueError(f"a prompt chunk holds 1..{self.max_rows} tokens (got {m})")
+        if not 0 <= seq < self.batch:
+            raise ValueError(f"sequence {seq} outside the batch of {self.batch}")
         with torch.cuda.device(self.device), torch.cuda.stream(self.stream):
-            self.tok[:m].copy_(torch.as_tensor(list(ids), dtype=torch.int64), non_blocking=False)
-            self._enqueue(m)
+            self.ids[:m].copy_(torch.as_tensor(list(ids), dtype=torch.int64), non_blocking=False)
+            self._enqueue(m, seq)
 
-    def reset(self, pos: int = 0) -> None:
-        """Set the position (and clear the error word) in order with the decoder's stream."""
+    def reset(self, pos=0) -> None:
+        """Set the positions (an int for every sequence, or one per sequence) and clear the error
+        word, in order with the decoder's stream."""
         with torch.cuda.device(self.device), torch.cuda.stream(self.stream):
-            self.pos.fill_(pos)
+            if isinstance(pos, int):
+                self.pos.fill_(pos)
+            else:
+                self.pos.copy_(torch.as_tensor(list(pos), dtype=torch.int32), non_blocking=False)
             self.err.zero_()
 
     def capture(self) -> None:
         """Record one token step as a CUDA graph (after one eager step that sets the kernels up;
-        the position is restored, and the cache rows that step wrote are rewritten later)."""
+        the positions are restored, and the cache rows that step wrote are rewritten later)."""
         with torch.cuda.device(self.device), torch.cuda.stream(self.stream):
             saved_tok, saved_pos = self.tok.clone(), self.pos.clone()
             self._enqueue_step()
@@ -328,8 +372,8 @@ class GemmaDecoder:
         self.graph = g
 
     def step(self) -> None:
-        """One token: embeds self.tok[0] at position self.pos, leaves the greedy next token in
-        self.tok[0] and the logits in self.logits, and advances self.pos."""
+        """One token per sequence: embeds self.tok[b] at position self.pos[b], leaves the greedy
+        next tokens in self.tok and the logits in self.logits, and advances every position."""
         with torch.cuda.device(self.device), torch.cuda.stream(self.stream):
             if self.graph is not None:
                 self.graph.replay()
@@ -341,24 +385,32 @@ class GemmaDecoder:
         self.stream.synchronize()
         e = int(self.err.item())
         if e:
-            self.reset(int(self.pos.item()))       # clears the error word on the decoder's stream
+            self.reset(self.pos.tolist())          # clears the error word on the decoder's stream
             raise RuntimeError({1: "token id outside the vocabulary",
                                 2: f"position outside the KV cache ({self.max_ctx})"}.get(e, f"error {e}"))
 
-    def generate(self, prompt: Sequence[int], n_new: int) -> List[int]:
-        """Greedy continuation of ``prompt`` (prefilled in chunks of max_prefill tokens)."""
-        if len(prompt) + n_new > self.max_ctx:
-            raise ValueError("prompt + new tokens exceed the KV cache")
+    def generate(self, prompt, n_new: int):
+        """Greedy continuation: ``prompt`` is one list of ids (batch 1; returns a list) or one
+        list per sequence of the batch (returns a list of lists). Prompts are prefilled in chunks
+        of max_prefill tokens, then all sequences decode together, one token each per step."""
+        single = len(prompt) == 0 or not isinstance(prompt[0], (list, tuple))
+        prompts = [list(prompt)] if single else [list(p) for p in prompt]
+        if len(prompts) != self.batch:
+            raise ValueError(f"{len(prompts)} prompts for a batch of {self.batch}")
+        if max(len(p) for p in prompts) + n_new > self.max_ctx or min(len(p) for p in prompts) < 1:
+            raise ValueError("prompt + new tokens exceed the KV cache (or a prompt is empty)")
         self.reset(0)
-        for i in range(0, len(prompt), self.max_rows):
-            self.prefill(prompt[i:i + self.max_rows])
-        out = []
+        for b, p in enumerate(prompts):
+            for i in range(0, len(p), self.max_rows):
+                self.prefill(p[i:i + self.max_rows], seq=b)
+        out = [[] for _ in prompts]
         for _ in range(n_new):
             self.stream.synchronize()
-            out.append(int(self.tok[0].item()))
+            for b, t in enumerate(self.tok.tolist()):
+                out[b].append(int(t))
             self.step()
         self.check()
-        return out
+        return out[0] if single else out
 
     def release(self) -> None:
         if self.graph is not None:

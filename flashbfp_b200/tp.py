@@ -139,23 +139,26 @@ class DecoderPlan:
 
 def argmax_slots(logits: torch.Tensor, vocab_offset: int, rank: int, world: int,
                  slots: torch.Tensor) -> None:
-    """Vocab-parallel greedy pick, first half: write this rank's (max logit, global index of its
-    first maximum) into slots [2 rank, 2 rank + 2) of the zeroed fp32 vector ``slots`` (2 world
-    values). Summing the ranks' vectors (any all-reduce) then gathers every rank's pair exactly:
-    each slot has one non-zero contributor, and indices below 2^24 are exact in fp32."""
-    val, idx = torch.max(logits.reshape(-1).float(), dim=0)
-    slots[2 * rank:2 * rank + 1].copy_(val.reshape(1))
-    slots[2 * rank + 1:2 * rank + 2].copy_((idx + vocab_offset).float().reshape(1))
+    """Vocab-parallel greedy pick, first half, for every row of ``logits`` (this rank's
+    vocabulary columns): write the row's (max logit, global index of its first maximum) into
+    slots [row, 2 rank : 2 rank + 2] of the zeroed fp32 ``slots`` (rows x 2 world values).
+    Summing the ranks' slots (any all-reduce) then gathers every rank's pair exactly: each slot
+    has one non-zero contributor, and indices below 2^24 are exact in fp32."""
+    lg = logits.reshape(-1, logits.shape[-1]).float()
+    val, idx = torch.max(lg, dim=-1)
+    sl = slots.view(lg.shape[0], 2 * world)
+    sl[:, 2 * rank].copy_(val)
+    sl[:, 2 * rank + 1].copy_((idx + vocab_offset).float())
 
 
-def argmax_pick(slots: torch.Tensor) -> torch.Tensor:
-    """Second half: the global index (int64, shape [1]) of the largest of the gathered maxima,
-    the lowest rank's on ties, which is the first maximum over the whole vocabulary because the
-    ranks hold ascending vocabulary ranges."""
-    pairs = slots.view(-1, 2)
-    # index_select keeps the pick on the device (indexing by a 0-d tensor would read it back
-    # to the host, which a CUDA graph capture does not allow)
-    return pairs[:, 1].index_select(0, torch.argmax(pairs[:, 0]).reshape(1)).long()
+def argmax_pick(slots: torch.Tensor, world: int) -> torch.Tensor:
+    """Second half: per row, the global index (int64) of the largest of the gathered maxima, the
+    lowest rank's on ties, which is the first maximum over the whole vocabulary because the ranks
+    hold ascending vocabulary ranges. Stays on the device (a gather, not indexing by a 0-d
+    tensor, which would read it back to the host and break a CUDA graph capture)."""
+    pairs = slots.view(-1, world, 2)
+    best = torch.argmax(pairs[..., 0], dim=-1, keepdim=True)
+    return pairs[..., 1].gather(1, best).reshape(-1).long()
 
 
 def all_reduce_sum(y: torch.Tensor, group=None, reducer: Optional["NVLinkAllReduce"] = None) -> torch.Tensor:

@@ -9,6 +9,8 @@ by weight distributions and layer shapes, which these generators reproduce.
   positions replaced by StudentT(df=3) * 20 * 0.02 (seed = base + layer id).
 * ``GEMMA12B_LAYER``: the linear shapes (out N x in K) of one 12B-class decoder
   layer: hidden 3840, 16 query heads and 8 KV heads of 256, GeGLU MLP 15360.
+* ``LLAMA70B_LAYER``: the same for the 70B-class stress layer: hidden 8192, 64 query heads
+  and 8 KV heads of 128, MLP 28672.
 
 Generators take a torch ``device`` so that large layers can be drawn directly
 in device memory.
@@ -28,6 +30,16 @@ GEMMA12B_LAYER = {
     "gate_proj": (15360, 3840),
     "up_proj": (15360, 3840),
     "down_proj": (3840, 15360),
+}
+# the 70B-class stress shapes: hidden 8192, 64 query / 8 KV heads of 128, MLP 28672
+LLAMA70B_LAYER = {
+    "q_proj": (8192, 8192),
+    "k_proj": (1024, 8192),
+    "v_proj": (1024, 8192),
+    "o_proj": (8192, 8192),
+    "gate_proj": (28672, 8192),
+    "up_proj": (28672, 8192),
+    "down_proj": (8192, 28672),
 }
 # fused launch groups used by decode: q|k|v and gate|up share their input
 GEMMA12B_FUSED = {

@@ -307,6 +307,17 @@ int fbfp_compress_outliers(const void* w, int w_dtype, int64_t n_out, int64_t k_
  *   max_ctx + 8 hd <= 10000, q and caches 16-byte aligned.
  * fbfp_geglu: out[r][i] = bf16(bf16(gelu_tanh(gate[r][i])) * up[r][i]) for rows [gate | up].
  * fbfp_advance_position: *pos += m.
+ *
+ * One new token per sequence (a batch of b sequences; b = 1 for a single one): row r is sequence
+ * r at its own position pos[r], with its own caches at k_cache + r * seq_stride (elements; at
+ * least nkv * max_ctx * hd apart).
+ * fbfp_decode_attention_step: fbfp_qk_rope_cache followed by fbfp_decode_attention for such rows
+ *   in one launch (the q/k norm, rotation and cache append folded into the attention, which is
+ *   split over positions in ranges of 64 and merged by the last CTA of each head and row); out
+ *   [b][nh][hd]. `scratch`: fbfp_decode_attention_step_scratch_bytes(b, nh, hd, max_ctx) bytes,
+ *   16-byte aligned and zeroed once before the first call (every call leaves its counters at
+ *   zero). A position outside [0, max_ctx) sets *err = 2 and skips that row.
+ * fbfp_advance_positions: pos[r] += 1 for r < b (1 <= b <= 1024).
  * ---------------------------------------------------------------------------------- */
 int fbfp_embed(const int64_t* tok, int64_t m, const void* table, int64_t vocab, int64_t hidden,
                float scale, void* out, int32_t* err, void* stream);
@@ -323,6 +334,14 @@ int fbfp_decode_attention(const void* q, int64_t m, const void* k_cache, const v
                           int64_t window, float scaling, void* out, void* stream);
 int fbfp_geglu(const void* gate_up, int64_t m, int64_t inter, void* out, void* stream);
 int fbfp_advance_position(int32_t* pos, int64_t m, void* stream);
+int64_t fbfp_decode_attention_step_scratch_bytes(int64_t b, int64_t nh, int64_t hd, int64_t max_ctx);
+int fbfp_decode_attention_step(const void* qkv, int64_t b, int64_t nh, int64_t nkv, int64_t hd,
+                               const void* q_norm_w, const void* k_norm_w, float eps,
+                               const void* cos_table, const void* sin_table, const int32_t* pos,
+                               int64_t max_ctx, void* k_cache, void* v_cache, int64_t seq_stride,
+                               int64_t window, float scaling, void* scratch, void* out, int32_t* err,
+                               void* stream);
+int fbfp_advance_positions(int32_t* pos, int64_t b, void* stream);
 
 #ifdef __cplusplus
 }

@@ -18,12 +18,12 @@ pytestmark = pytest.mark.gpu
 T = 24
 
 
-def _tiny(seed):
+def _tiny(seed, sliding_window=4, max_pos=128):
     transformers = pytest.importorskip("transformers")
     cfg = transformers.Gemma3TextConfig(vocab_size=512, hidden_size=256, intermediate_size=512,
                                         num_hidden_layers=2, num_attention_heads=4,
                                         num_key_value_heads=2, head_dim=64,
-                                        max_position_embeddings=128, sliding_window=4,
+                                        max_position_embeddings=max_pos, sliding_window=sliding_window,
                                         layer_types=["sliding_attention", "full_attention"],
                                         attn_implementation="eager")
     torch.manual_seed(seed)
@@ -129,3 +129,81 @@ def test_position_past_the_cache_is_reported():
         dec.check()
     with pytest.raises(ValueError, match="exceed"):
         dec.generate([1, 2, 3], 6)
+
+
+def test_long_context_split_attention_matches_hugging_face():
+    """150 positions (the token step's attention splits them over three CTAs per head and
+    merges), a sliding window of 100 that starts inside a range: per-position logits of the
+    step-by-step decode against Hugging Face over the whole sequence."""
+    from flashbfp_b200 import OABFCompressor
+    from flashbfp_b200.decode import GemmaDecoder
+    from flashbfp_b200.model import compress_gemma_model
+    dev = torch.device("cuda", 0)
+    n = 150
+    model = compress_gemma_model(_tiny(3, 100, 256).to(dev, torch.bfloat16), OABFCompressor())
+    ref = _dequantised_reference(_tiny(3, 100, 256).to(dev, torch.bfloat16))
+    ids = torch.randint(0, 512, (n,), generator=torch.Generator().manual_seed(8)).tolist()
+    dec = GemmaDecoder.from_hf(model, max_ctx=160, max_prefill=8)
+    ours = _run(dec, ids)
+    with torch.no_grad():
+        want = ref(torch.tensor([ids], device=dev)).logits[0].float()
+    for i in range(n):
+        rel = ((ours[i] - want[i]).norm() / want[i].norm()).item()
+        assert rel <= 2e-2, (i, rel)
+    dec.release()
+
+
+def test_batch_decode_matches_single_sequences():
+    """Three sequences of different prompt lengths decoding together (one row each, at their own
+    positions, in their own caches): teacher-forced, every sequence's logits equal those of the
+    same sequence decoded alone (up to the order of fp32 sums in the batched lm_head), eager and
+    replayed from the CUDA graph; generate() on the batch returns per-sequence continuations."""
+    from flashbfp_b200 import OABFCompressor
+    from flashbfp_b200.decode import GemmaDecoder
+    from flashbfp_b200.model import compress_gemma_model
+    dev = torch.device("cuda", 0)
+    model = compress_gemma_model(_tiny(4, 8).to(dev, torch.bfloat16), OABFCompressor())
+    g = torch.Generator().manual_seed(12)
+    prompts = [torch.randint(0, 512, (L,), generator=g).tolist() for L in (5, 19, 2)]
+    follow = [torch.randint(0, 512, (10,), generator=g).tolist() for _ in prompts]
+    single = GemmaDecoder.from_hf(model, max_ctx=48, max_prefill=16)
+    alone = []
+    for p, f in zip(prompts, follow):
+        single.reset(0)
+        for i in range(0, len(p), 16):
+            single.prefill(p[i:i + 16])
+        got = []
+        for t in f:
+            with torch.cuda.stream(single.stream):
+                single.tok.fill_(int(t))
+            single.step()
+            single.stream.synchronize()
+            got.append(single.logits[0].float().clone())
+        single.check()
+        alone.append(torch.stack(got))
+    batch = GemmaDecoder.from_hf(model, max_ctx=48, max_prefill=16, batch=3)
+    assert batch.k_cache.shape[1] == 3 and batch.pos.shape == (3,)
+    for mode in ("eager", "graph"):
+        if mode == "graph":
+            batch.capture()
+        batch.reset(0)
+        for b, p in enumerate(prompts):
+            for i in range(0, len(p), 16):
+                batch.prefill(p[i:i + 16], seq=b)
+        assert batch.pos.tolist() == [len(p) for p in prompts]
+        for s_ in range(10):
+            with torch.cuda.stream(batch.stream):
+                batch.tok.copy_(torch.tensor([f[s_] for f in follow], device=dev))
+            batch.step()
+            batch.stream.synchronize()
+            for b in range(3):
+                want = alone[b][s_]
+                rel = ((batch.logits[b].float() - want).norm() / want.norm()).item()
+                assert rel <= 1e-2, (mode, s_, b, rel)
+        batch.check()
+    outs = batch.generate(prompts, 4)
+    assert len(outs) == 3 and all(len(o) == 4 and all(0 <= t < 512 for t in o) for o in outs)
+    with pytest.raises(ValueError):
+        batch.generate(prompts[:2], 4)
+    batch.release()
+    single.release()

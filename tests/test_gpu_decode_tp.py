@@ -82,7 +82,7 @@ def _worker(rank, port, q):
                                          rank=rank, world=WORLD)
             ar = NVLinkAllReduce(32 * 256)
             dec = GemmaDecoder.from_hf(model, max_ctx=64, max_prefill=32, reducer=ar)
-            assert dec.hq == 2 and dec.hkv == 1 and dec.k_cache.shape[1] == 1
+            assert dec.hq == 2 and dec.hkv == 1 and dec.k_cache.shape[2] == 1
             assert dec.fused_rows == (head_dim == 128)
             for mode in ("eager", "graph"):
                 if mode == "graph":

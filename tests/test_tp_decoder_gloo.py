@@ -110,7 +110,7 @@ def _worker(rank, world, port, q):
         slots = torch.zeros(2 * world, dtype=torch.float32)
         tp.argmax_slots(logits, v0, rank, world, slots)
         dist.all_reduce(slots)
-        assert int(tp.argmax_pick(slots)) == tok_full
+        assert int(tp.argmax_pick(slots, world)) == tok_full
         # ties across ranks resolve to the lowest global index, as one argmax would
         tie = torch.zeros(v1 - v0)
         tie[-1] = 1.0
@@ -118,7 +118,7 @@ def _worker(rank, world, port, q):
         tp.argmax_slots(tie, v0, rank, world, slots)
         dist.all_reduce(slots)
         # every rank's maximum sits on its last row: the first over the vocabulary is rank 0's
-        assert int(tp.argmax_pick(slots)) == tp.DecoderPlan(NH, NKV, HD, INTER, VOCAB, 0, world).vocab[1] - 1
+        assert int(tp.argmax_pick(slots, world)) == tp.DecoderPlan(NH, NKV, HD, INTER, VOCAB, 0, world).vocab[1] - 1
         q.put((rank, "ok"))
     except Exception as e:                      # reported to the parent, which fails the test
         q.put((rank, repr(e)))
