@@ -51,6 +51,14 @@ __device__ __forceinline__ uint32_t float_to_bf16_bits(float f) {
 __device__ __forceinline__ float round_bf16(float f) {
   return bf16_bits_to_float(float_to_bf16_bits(f));
 }
+// Two values rounded to bf16 (nearest even) by one paired conversion; same results as
+// round_bf16 on each.
+__device__ __forceinline__ void round_bf16x2(float& a, float& b) {
+  const __nv_bfloat162 h = __float22bfloat162_rn(make_float2(a, b));
+  const uint32_t u = *reinterpret_cast<const uint32_t*>(&h);
+  a = __uint_as_float(u << 16);
+  b = __uint_as_float(u & 0xFFFF0000u);
+}
 __device__ __forceinline__ float load_as_float(const void* p, int dtype, int64_t i) {
   if (dtype == FBFP_F32) return reinterpret_cast<const float*>(p)[i];
   if (dtype == FBFP_BF16)

@@ -122,6 +122,65 @@ stats_mean_kernel(const double* parts, int nparts, int64_t numel, int dt, StatsH
   }
 }
 
+// bf16 weights: the same two sums with the per-element work in fp32 and fp64 only once per 8
+// elements. The fourth-power term is computed exactly as the fp64 route computes it: d is a
+// bf16 value, so d*d is exact in fp32 and d^4 = (d*d)^2 is one fp32 rounding of the exact
+// product, which is what rounding the exact fp64 product to fp32 gives. The centred square
+// sum uses the fp32 shift mh = fl32(mean): sum((x - m)^2) = S2 - 2 dm S1 + N dm^2 with
+// S1 = sum(x - mh), S2 = sum((x - mh)^2) and dm = m - mh, taken in fp64 at the end
+// (stats_threshold_kernel); each 8-element fp32 partial is added to an fp64 accumulator, so
+// the rounding errors of the partials are independent, unbiased and about 2^-24 of a partial:
+// their sum is far below one rounding step of the bf16 (or fp32) variance.
+__global__ void __launch_bounds__(kStatThreads)
+stats_central_bf16_kernel(const void* w, int64_t n_out, int64_t k_in, int64_t ldw,
+                          const StatsHeader* hdr, double* parts) {
+  const float mh = __double2float_rn(hdr->mean64);
+  const float mdt = hdr->mean_dt;
+  double acc[3] = {0.0, 0.0, 0.0};                // S2, fourth-power sum, S1
+  const int lane = threadIdx.x & 31;
+  const int64_t warp = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 5;
+  const int64_t nwarps = ((int64_t)gridDim.x * blockDim.x) >> 5;
+  for (int64_t n = warp; n < n_out; n += nwarps) {
+    const uint16_t* row = reinterpret_cast<const uint16_t*>(w) + n * ldw;
+    const bool vec = ((uintptr_t)row & 15) == 0;
+    for (int64_t k0 = (int64_t)lane * 8; k0 < k_in; k0 += 256) {
+      float v[8];
+      int cnt = 8;
+      if (vec && k0 + 8 <= k_in) {
+        const uint4 q = *reinterpret_cast<const uint4*>(row + k0);
+        const uint32_t u[4] = {q.x, q.y, q.z, q.w};
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          v[2 * j] = __uint_as_float(u[j] << 16);
+          v[2 * j + 1] = __uint_as_float(u[j] & 0xFFFF0000u);
+        }
+      } else {
+        cnt = (int)(k_in - k0 < 8 ? k_in - k0 : 8);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) v[j] = j < cnt ? bf16_bits_to_float(row[k0 + j]) : mh;
+      }
+      float s1 = 0.f, s2 = 0.f, s4 = 0.f;
+#pragma unroll
+      for (int j = 0; j < 8; j += 2) {
+        const float t0 = __fsub_rn(v[j], mh), t1 = __fsub_rn(v[j + 1], mh);
+        s1 = __fadd_rn(__fadd_rn(s1, t0), t1);
+        s2 = __fmaf_rn(t1, t1, __fmaf_rn(t0, t0, s2));
+        float d0 = __fsub_rn(v[j], mdt), d1 = __fsub_rn(v[j + 1], mdt);
+        round_bf16x2(d0, d1);                                   // (W - mean) in bf16
+        const float e0 = __fmul_rn(d0, d0), e1 = __fmul_rn(d1, d1);    // exact
+        float p0 = __fmul_rn(e0, e0), p1 = __fmul_rn(e1, e1);
+        round_bf16x2(p0, p1);                                   // ** 4 in bf16
+        s4 = j < cnt ? __fadd_rn(s4, p0) : s4;
+        s4 = j + 1 < cnt ? __fadd_rn(s4, p1) : s4;
+      }
+      acc[0] += (double)s2;
+      acc[1] += (double)s4;
+      acc[2] += (double)s1;
+    }
+  }
+  block_reduce_store<3>(acc, parts);
+}
+
 __global__ void __launch_bounds__(kStatThreads)
 stats_central_kernel(const void* w, int dt, int64_t n_out, int64_t k_in, int64_t ldw,
                      const StatsHeader* hdr, double* parts) {
@@ -142,9 +201,14 @@ stats_central_kernel(const void* w, int dt, int64_t n_out, int64_t k_in, int64_t
 // Scalar chain of compute_dynamic_threshold (compressor.py:19-32), rounded like torch.
 __global__ void __launch_bounds__(1024)
 stats_threshold_kernel(const double* parts, int nparts, int64_t numel, int dt, StatsHeader* hdr,
-                       float* thr_out) {
-  const double s2 = reduce_parts(parts, nparts);
+                       float* thr_out, int shifted) {
+  double s2 = reduce_parts(parts, nparts);
   const double s4 = reduce_parts(parts + kStatParts, nparts);
+  if (shifted) {                                  // sums about mh = fl32(mean): recentre on the mean
+    const double s1 = reduce_parts(parts + 2 * kStatParts, nparts);
+    const double dm = hdr->mean64 - (double)__double2float_rn(hdr->mean64);
+    s2 = s2 - 2.0 * dm * s1 + (double)numel * dm * dm;
+  }
   if (threadIdx.x != 0) return;
   hdr->s2 = s2;
   hdr->s4 = s4;
@@ -242,16 +306,23 @@ pack_kernel(const void* w, int dt, int64_t n_out, int64_t k_in, int64_t ldw, int
     const float xm = fmaxf(bmax, c1e8);
     const int e = floor_log2_torch(xm, dt);
     const bool unit = bmax < c1e7;                            // scale = 1 for tiny blocks
-    const float inv = unit ? 1.0f : __uint_as_float((uint32_t)(127 - e) << 23);  // 2^-e, exact
+    // 15 * 2^-e, exact (e >= -27 unless the block is tiny, where the scale is 1): one rounding
+    // of |x| * 15 / 2^e equals the reference's rounding of (|x| / 2^e, exact) * 15
+    const float inv15 = unit ? 15.0f : __uint_as_float((uint32_t)(127 - e) << 23) * 15.0f;
     uint32_t s = 0, w0 = 0, w1 = 0;
+    float q[16];
+#pragma unroll
+    for (int j = 0; j < 16; ++j) q[j] = __fmul_rn(fabsf(v[j]), inv15);
+    if (dt == FBFP_BF16) {
+#pragma unroll
+      for (int j = 0; j < 16; j += 2) round_bf16x2(q[j], q[j + 1]);
+    }
 #pragma unroll
     for (int j = 0; j < 16; ++j) {
-      const float al = fabsf(v[j]) * inv;                     // |x| / 2^e, exact
-      float q = __fmul_rn(al, 15.0f);
-      q = rnd_dt(q, dt);
-      float r = rintf(q);                                     // round half to even
-      r = fminf(fmaxf(r, 0.f), 15.f);
-      const uint32_t m = (uint32_t)r;
+      // 0 <= q < 30: adding 1.5 * 2^23 rounds q half-to-even to an integer held in the low
+      // mantissa bits; clamp to 15
+      const uint32_t r = __float_as_uint(__fadd_rn(q[j], 12582912.0f)) - 0x4B400000u;
+      const uint32_t m = r < 15u ? r : 15u;
       if (j < 8) w0 |= m << (4 * j); else w1 |= m << (4 * (j - 8));
       if (v[j] < 0.f) s |= 1u << j;
     }
@@ -259,11 +330,16 @@ pack_kernel(const void* w, int dt, int64_t n_out, int64_t k_in, int64_t ldw, int
     sg[b] = (int16_t)(uint16_t)s;
     pay[b] = make_uint2(w0, w1);
     masks[b] = (uint16_t)omask;
-    if (omask) atomicAdd(&row_counts[n], __popc(omask));
+    // one atomic per row a warp touches (a warp's 32 consecutive blocks span one or two rows)
+    const unsigned act = __activemask();
+    const unsigned same = __match_any_sync(act, (unsigned long long)n);
+    const int tot = __reduce_add_sync(same, __popc(omask));
+    if (tot && (threadIdx.x & 31) == __ffs(same) - 1) atomicAdd(&row_counts[n], tot);
   }
 }
 
-// One warp per padded row: ordered compaction of the outlier bits of the row's blocks.
+// One warp per padded row: ordered compaction of the outlier bits of the row's blocks (the
+// row's block masks are read 8 chunks of 32 at a time, so their loads overlap).
 __global__ void __launch_bounds__(256)
 emit_outliers_kernel(const void* w, int dt, int64_t n_out, int64_t ldw, int64_t kb_row,
                      const uint16_t* masks, const int32_t* row_offsets, int32_t* bidx,
@@ -276,9 +352,20 @@ emit_outliers_kernel(const void* w, int dt, int64_t n_out, int64_t ldw, int64_t 
     int64_t base = row_offsets[n];
     if (row_offsets[n + 1] == base) continue;
     const char* row = reinterpret_cast<const char*>(w) + n * ldw * es;
+    uint32_t mk[8];                              // the next 8 chunks' masks, loaded together
     for (int64_t kb0 = 0; kb0 < kb_row; kb0 += 32) {
       const int64_t kb = kb0 + lane;
-      const uint32_t m = kb < kb_row ? masks[n * kb_row + kb] : 0u;
+      const int ci = (int)((kb0 >> 5) & 7);
+      if (ci == 0) {
+#pragma unroll
+        for (int c8 = 0; c8 < 8; ++c8) {
+          const int64_t kk = kb + 32 * c8;
+          mk[c8] = kk < kb_row ? masks[n * kb_row + kk] : 0u;
+        }
+      }
+      uint32_t m = mk[0];
+#pragma unroll
+      for (int c8 = 1; c8 < 8; ++c8) m = ci == c8 ? mk[c8] : m;
       const int c = __popc(m);
       int incl = c;
       for (int o = 1; o < 32; o <<= 1) {
@@ -317,7 +404,7 @@ static ScratchLayout scratch_layout(int64_t kpad, int64_t npad) {
   ScratchLayout L;
   L.hdr = 0;
   L.parts = align256(sizeof(StatsHeader));
-  L.masks = L.parts + align256(sizeof(double) * 2 * kStatParts);
+  L.masks = L.parts + align256(sizeof(double) * 3 * kStatParts);
   L.total = L.masks + align256(sizeof(uint16_t) * (size_t)(npad * (kpad / kBlock)));
   return L;
 }
@@ -348,9 +435,15 @@ extern "C" int fbfp_compress_threshold(const void* w, int w_dtype, int64_t n_out
   FBFP_LAUNCH_CHECK("stats_sum_kernel");
   stats_mean_kernel<<<1, 1024, 0, st>>>(parts, grid, numel, w_dtype, hdr);
   FBFP_LAUNCH_CHECK("stats_mean_kernel");
-  stats_central_kernel<<<grid, kStatThreads, 0, st>>>(w, w_dtype, n_out, k_in, ldw, hdr, parts);
-  FBFP_LAUNCH_CHECK("stats_central_kernel");
-  stats_threshold_kernel<<<1, 1024, 0, st>>>(parts, grid, numel, w_dtype, hdr, thr_out);
+  const int shifted = w_dtype == FBFP_BF16;
+  if (shifted) {
+    stats_central_bf16_kernel<<<grid, kStatThreads, 0, st>>>(w, n_out, k_in, ldw, hdr, parts);
+    FBFP_LAUNCH_CHECK("stats_central_bf16_kernel");
+  } else {
+    stats_central_kernel<<<grid, kStatThreads, 0, st>>>(w, w_dtype, n_out, k_in, ldw, hdr, parts);
+    FBFP_LAUNCH_CHECK("stats_central_kernel");
+  }
+  stats_threshold_kernel<<<1, 1024, 0, st>>>(parts, grid, numel, w_dtype, hdr, thr_out, shifted);
   FBFP_LAUNCH_CHECK("stats_threshold_kernel");
   return FBFP_OK;
 }
