@@ -315,18 +315,21 @@ def run_ours(args):
             dist.barrier()
     _progress(rank, "timed steps done")
     elapsed_ms = start.elapsed_time(stop)
-    # per-kind rates (all 48 launches of one kind back to back), outside the headline timing
+    # per-kind rates (all 48 launches of one kind back to back), outside the headline timing;
+    # each kind's timed replays follow one untimed replay, which (for the kinds that exchange
+    # with the other ranks) lines the ranks up, so no rank's timing absorbs another's late start
     Kk = max(1, K // 4)
-    ev = [[torch.cuda.Event(enable_timing=True) for _ in range(len(KINDS) + 1)] for _ in range(Kk)]
+    kind_ms = {}
     with torch.cuda.stream(stream):
-        for s in range(Kk):
-            ev[s][0].record(stream)
-            for i, kk in enumerate(KINDS):
+        for kk in KINDS:
+            graphs[kk].replay()
+            a_ev, b_ev = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a_ev.record(stream)
+            for _ in range(Kk):
                 graphs[kk].replay()
-                ev[s][i + 1].record(stream)
-    torch.cuda.synchronize(device)
-    kind_ms = {kk: sum(ev[s][i].elapsed_time(ev[s][i + 1]) for s in range(Kk)) / Kk
-               for i, kk in enumerate(KINDS)}
+            b_ev.record(stream)
+            b_ev.synchronize()
+            kind_ms[kk] = a_ev.elapsed_time(b_ev) / Kk
     t = torch.tensor([elapsed_ms] + [kind_ms[kk] for kk in KINDS], dtype=torch.float64, device=device)
     if world > 1:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
@@ -813,25 +816,21 @@ def time_linear_step(layers, m, device, world, reducer, steps):
     torch.cuda.synchronize(device)
     if world > 1:
         dist.barrier()
-    ev = [torch.cuda.Event(enable_timing=True) for _ in range(6)]
     kreps = max(1, steps // 4)
+    t = []
     with torch.cuda.stream(st):
-        ev[0].record(st)
-        for _ in range(steps):
-            g.replay()
-        ev[1].record(st)
-        for i, kk in enumerate(KINDS):
-            for _ in range(kreps):
-                graphs[kk].replay()
-            ev[2 + i].record(st)
+        for gg, reps in [(g, steps)] + [(graphs[kk], kreps) for kk in KINDS]:
+            gg.replay()                         # untimed: lines the ranks up
+            a_ev, b_ev = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a_ev.record(st)
+            for _ in range(reps):
+                gg.replay()
+            b_ev.record(st)
+            b_ev.synchronize()
+            t.append(a_ev.elapsed_time(b_ev) / reps)
     torch.cuda.synchronize(device)
     for kk in KINDS:
         _lib.check(L.fbfp_gemv_check(_lib.ptr(ws[kk]), _lib.stream_ptr(device)), "fbfp_gemv_check")
-    t = [ev[0].elapsed_time(ev[1]) / steps]
-    prev = ev[1]
-    for i in range(len(KINDS)):
-        t.append(prev.elapsed_time(ev[2 + i]) / kreps)
-        prev = ev[2 + i]
     tt = torch.tensor(t, dtype=torch.float64, device=device)
     if world > 1:
         dist.all_reduce(tt, op=dist.ReduceOp.MAX)

@@ -11,11 +11,14 @@
 //                                it) and error word
 //   slots[2][kMaxWorld][max_elems] {uint32 value bits, uint32 tag}: slot [parity][src] holds
 //                                src's partial of the call with that parity
-// A call with epoch e (parity e & 1, tag e + 1), one CTA:
+// A call with epoch e (parity e & 1, tag e + 1), one CTA per 8192 elements, each on its own
+// contiguous chunk (the same chunks on every rank, as n is the same):
 //   1. write {y[i], tag} into slot [parity][rank] of every rank (peers through NVLink);
 //   2. for every element and every rank q in rank order, wait (bounded) until the local slot
 //      [parity][q] carries tag, and add its value (fixed order: every rank gets the same bits);
-//   3. epoch = tag.
+//   3. the last CTA to finish (a counter in the header) sets epoch = tag, unless a wait gave up.
+// A CTA waits only for the peers' CTAs of its own chunk, never for another CTA of its rank, so
+// the chunks progress independently whatever the CTAs' residency.
 // Reusing a parity two calls later is safe: a rank starts call e + 2 only after it has received
 // every peer's words of call e + 1, which peers sent after finishing call e (stream order). Every
 // wait is bounded (two seconds by default, fbfp_allreduce_set_timeout): then the kernel records an
@@ -56,6 +59,9 @@ struct ArArgs {
 
 __device__ __forceinline__ uint32_t* ar_epoch(uint8_t* b) { return xchg_epoch(b); }
 __device__ __forceinline__ int32_t* ar_err(uint8_t* b) { return xchg_err(b); }
+// CTAs of the current call that have finished (header word 2; the last one resets it)
+__device__ __forceinline__ int32_t* ar_exit(uint8_t* b) { return reinterpret_cast<int32_t*>(b + 8); }
+constexpr int64_t kArChunk = 8192;
 __device__ __forceinline__ uint2* ar_slot(uint8_t* b, int64_t max_elems, uint32_t par, int src) {
   return xchg_slot(b, max_elems, par, src);
 }
@@ -71,15 +77,17 @@ __global__ void __launch_bounds__(kArThreads, 1) allreduce_sum_kernel(const ArAr
   if (tid == 0) { s_epoch = *ar_epoch(a.self); s_fail = 0; }
   __syncthreads();
   const uint32_t e = s_epoch, par = e & 1u, tag = e + 1u;
+  const int64_t c0 = (int64_t)blockIdx.x * kArChunk;
+  const int64_t c1 = c0 + kArChunk < a.n ? c0 + kArChunk : a.n;
   // 1. push {value, tag} words into slot [par][rank] of every rank
   for (int p = 0; p < a.world; ++p) {
     uint2* dst = ar_slot(a.peer[p], a.max_elems, par, a.rank);
-    for (int64_t i = tid; i < a.n; i += kArThreads) st_word(dst + i, __float_as_uint(a.y[i]), tag);
+    for (int64_t i = c0 + tid; i < c1; i += kArThreads) st_word(dst + i, __float_as_uint(a.y[i]), tag);
   }
   // 2. receive and sum in rank order (each thread its own elements); a wait that gives up (after
   // a.timeout_ns of the global timer) sets s_fail, and every thread then skips to the barrier
   bool stop = false;
-  for (int64_t i = tid; i < a.n && !stop; i += kArThreads) {
+  for (int64_t i = c0 + tid; i < c1 && !stop; i += kArThreads) {
     float acc = 0.f;
     for (int q = 0; q < a.world && !stop; ++q) {
       const uint2* src = ar_slot(a.self, a.max_elems, par, q) + i;
@@ -105,7 +113,13 @@ __global__ void __launch_bounds__(kArThreads, 1) allreduce_sum_kernel(const ArAr
     if (!stop) a.y[i] = acc;
   }
   __syncthreads();
-  if (tid == 0 && !s_fail) *ar_epoch(a.self) = tag;    // 3.
+  if (tid == 0) {                                        // 3.
+    __threadfence();
+    if (atomicAdd(ar_exit(a.self), 1) == (int)gridDim.x - 1) {
+      *ar_exit(a.self) = 0;
+      if (*reinterpret_cast<volatile int32_t*>(ar_err(a.self)) == 0) *ar_epoch(a.self) = tag;
+    }
+  }
 }
 
 static size_t ar_bytes(int64_t max_elems) {
@@ -195,7 +209,7 @@ extern "C" int fbfp_allreduce_sum_f32(void* handle, float* y, int64_t n, void* s
   // programmatic stream serialisation: the launch overlaps the previous kernel's drain; the
   // kernel waits for it (griddepcontrol.wait) before reading anything
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(1);
+  cfg.gridDim = dim3((unsigned)((n + kArChunk - 1) / kArChunk));
   cfg.blockDim = dim3(kArThreads);
   cfg.dynamicSmemBytes = 0;
   cfg.stream = as_stream(stream);
