@@ -133,3 +133,35 @@ class OABFCompressor:
         dense_payload = {k: (v.cpu() if isinstance(v, torch.Tensor) else v) for k, v in dp.items()}
         sparse_outliers = {k: (v.cpu() if isinstance(v, torch.Tensor) else v) for k, v in sp.items()}
         return dense_payload, sparse_outliers
+
+
+def _main(argv=None) -> None:
+    """``python -m flashbfp_b200.compressor [N K [reps]]``: time ``compress_matrix_device`` on a
+    seeded N x K bf16 weight (N(0, 0.02) with 1.5% heavy-tailed outliers) on the current GPU,
+    after two warm-up calls; prints the time per call and the bytes moved per second."""
+    import json
+    import sys
+    from . import workloads
+    args = [int(a) for a in (sys.argv[1:] if argv is None else argv)]
+    n, k = (args[0], args[1]) if len(args) >= 2 else (30720, 3840)
+    reps = args[2] if len(args) >= 3 else 5
+    dev = torch.device("cuda", torch.cuda.current_device())
+    W = workloads.decode_weight(n, k, seed=21, device=dev)
+    comp = OABFCompressor()
+    for _ in range(2):
+        dp, sp = comp.compress_matrix_device(W)
+    torch.cuda.synchronize(dev)
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    for _ in range(reps):
+        dp, sp = comp.compress_matrix_device(W)
+    b.record()
+    torch.cuda.synchronize(dev)
+    ms = a.elapsed_time(b) / reps
+    alg = 2.0 * n * k + 11.0 * dp["exponents"].numel() + 10.0 * int(sp["count"])
+    print(json.dumps({"shape": [n, k], "ms": round(ms, 4), "input_gbs": round(2.0 * n * k / ms / 1e6, 1),
+                      "algorithmic_gbs": round(alg / ms / 1e6, 1), "outliers": int(sp["count"])}))
+
+
+if __name__ == "__main__":
+    _main()
