@@ -39,6 +39,7 @@ constexpr int kOutOff = kExpOff + 128 * 16;     // stage's outlier entries (wind
 constexpr int kOutCap = 1024;
 constexpr int kRoffOff = kOutOff + kOutCap * 4; // 136 uint16 row starts
 constexpr int kRoffBytes = 272;
+constexpr int kRangeOff = kRoffOff + 512;       // the stage's PfRange, written by the producer
 constexpr int kWStageBytes = kRoffOff + 1024;   // 27 KB
 constexpr uint32_t kWeightTx = kOutOff;
 constexpr int kBN = 256;                        // tokens per tile
@@ -151,10 +152,12 @@ __device__ void pf_producer_thread(const PfShared& S, const PfArgs& a, const PfM
   for (int64_t t = blockIdx.x; t < a.n_tiles && ok; t += gridDim.x) {
     const int rg = (int)(t / a.n_tt), tt = (int)(t % a.n_tt);
     for (int st = 0; st < a.n_stages && ok; ++st) {
-      if (!(ok = pf_wait(S, a, &S.wempty[ws], wph ^ 1, 1))) break;
       const int64_t seg = (int64_t)rg * a.n_stages + st;
-      const PfRange orr = pf_range(a, seg);
+      const PfRange orr = pf_range(a, seg);          // its loads overlap the wait below
+      if (!(ok = pf_wait(S, a, &S.wempty[ws], wph ^ 1, 1))) break;
       uint8_t* sb = S.wst + (size_t)ws * pf::kWStageBytes;
+      // the dequantisers read the range here, after the stage's full barrier
+      *reinterpret_cast<int4*>(sb + pf::kRangeOff) = make_int4(orr.lo, orr.lo4, orr.n, 0);
       mbar_arrive_expect_tx(&S.wfull[ws], pf::kWeightTx + (uint32_t)orr.n * 4 +
                                               (a.entries ? pf::kRoffBytes : 0));
       tma_2d_g2s(sb + pf::kPayOff, &M.pay, st * 128, rg * 128, &S.wfull[ws]);
@@ -279,7 +282,8 @@ __device__ void pf_dequant(const PfShared& S, const PfArgs& a, uint32_t tmem) {
       if (a.entries && rvalid) {
         // outliers of this row in this substage's 64 columns go into their +0 slots as
         // bf16(15 v): the epilogue's 1/15 scale then yields v * x
-        const PfRange orr = pf_range(a, (int64_t)rg * a.n_stages + st);
+        const int4 rr = *reinterpret_cast<const int4*>(sb + pf::kRangeOff);
+        const PfRange orr{rr.x, rr.y, rr.z};
         const uint16_t* ro = reinterpret_cast<const uint16_t*>(sb + pf::kRoffOff);
         const uint32_t* es = reinterpret_cast<const uint32_t*>(sb + pf::kOutOff);
         const int e_end = ro[lr + 1];
