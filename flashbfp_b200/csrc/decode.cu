@@ -394,9 +394,10 @@ decode_attention_kernel(const bf16* q, const bf16* kc, const bf16* vc, int nh, i
 // the q/k RMSNorm, the rotary embedding and the KV-cache append of fbfp_qk_rope_cache folded in,
 // and split over positions: CTA (head, row, split) covers the cached positions
 // [split * kFaChunk, (split + 1) * kFaChunk) of the row's window [lo, p]. It loads its cached
-// keys and values first (the loads overlap the norms), normalises and rotates its query head;
-// the CTAs whose range holds p compute the new key and value (the first query head of each KV
-// group also writes them to the cache) and use them from shared memory. Each CTA writes its
+// keys and values first (the loads overlap the norms); every warp normalises and rotates the
+// query head in registers; in the CTAs whose range holds p every warp also computes the new key
+// and value (one warp of the first query head of each KV group writes them to the cache) and
+// uses them from registers. Each CTA writes its
 // softmax partial (max, sum, weighted values) to scratch; the last of a (head, row)'s CTAs to
 // finish (an atomic count) merges them and returns the counter to zero for the next launch.
 // Same arithmetic as the two separate kernels (bf16 roundings of the norm and the rotation, fp32
@@ -404,26 +405,59 @@ decode_attention_kernel(const bf16* q, const bf16* kc, const bf16* vc, int nh, i
 constexpr int kFaThreads = 256;
 constexpr int kFaChunk = 64;
 
-// Normalise (RMSNorm over hd with weights 1 + w) and rotate one head of a fused q|k|v row into
-// dst (fp32 values that are bf16-rounded as the separate kernel rounds them). Every thread of
-// the CTA calls it; uses red (33 floats) and tmp (hd floats).
-__device__ void fa_norm_rope(const bf16* x, const bf16* w, float eps, int hd, const bf16* cr, const bf16* sr,
-                             float* tmp, float* red, float* dst) {
+// One warp: RMSNorm (weights 1 + w) and rotation of one head of hd (a multiple of 16, at most
+// 256) values of a fused q|k|v row, lane l owning dims 8l .. 8l + 7 (lanes past hd / 8 hold
+// zeros): the sum of squares is a warp reduction, and the rotation's partner of dim d (d +- hd/2)
+// sits hd / 16 lanes away. Rounded to bf16 where the separate kernel rounds: the normalised
+// value, each product, their sum.
+__device__ __forceinline__ void fa_warp_norm_rope(const bf16* x, const bf16* w, float eps, int hd,
+                                                  const bf16* cr, const bf16* sr, float (&v)[8]) {
+  const int lane = threadIdx.x & 31;
+  const bool act = lane * 8 < hd;
+  float xv[8], wv[8], t[8];
+  if (act) {
+    unpack8(*reinterpret_cast<const uint4*>(x + lane * 8), xv);
+    unpack8(*reinterpret_cast<const uint4*>(w + lane * 8), wv);
+  } else {
+#pragma unroll
+    for (int i = 0; i < 8; ++i) xv[i] = wv[i] = 0.f;
+  }
   float ss = 0.f;
-  for (int d = threadIdx.x; d < hd; d += blockDim.x) {
-    const float v = ldb(x + d);
-    tmp[d] = v;
-    ss += v * v;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) ss += xv[i] * xv[i];
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+  const float r = rsqrtf(ss / (float)hd + eps);
+#pragma unroll
+  for (int i = 0; i < 8; ++i) t[i] = bfr(xv[i] * r * (1.f + wv[i]));
+  const int hl = hd >> 4;                         // lanes per half of the head
+  const bool lo_half = lane < hl;
+  const int partner = lo_half ? lane + hl : lane - hl;
+  float cv[8], sv[8];
+  if (act) {
+    unpack8(*reinterpret_cast<const uint4*>(cr + lane * 8), cv);
+    unpack8(*reinterpret_cast<const uint4*>(sr + lane * 8), sv);
+  } else {
+#pragma unroll
+    for (int i = 0; i < 8; ++i) cv[i] = sv[i] = 0.f;
   }
-  const float r = rsqrtf(block_sum(ss, red) / (float)hd + eps);
-  for (int d = threadIdx.x; d < hd; d += blockDim.x) tmp[d] = bfr(tmp[d] * r * (1.f + ldb(w + d)));
-  __syncthreads();
-  const int half = hd / 2;
-  for (int d = threadIdx.x; d < hd; d += blockDim.x) {
-    const float rot = d < half ? -tmp[d + half] : tmp[d - half];
-    dst[d] = bfr(bfr(tmp[d] * ldb(cr + d)) + bfr(rot * ldb(sr + d)));
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const float pv = __shfl_sync(0xffffffffu, t[i], partner & 31);
+    const float rot = lo_half ? -pv : pv;
+    v[i] = act ? bfr(bfr(t[i] * cv[i]) + bfr(rot * sv[i])) : 0.f;
   }
-  __syncthreads();
+}
+
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  return v;
+}
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
 }
 
 __global__ void __launch_bounds__(kFaThreads)
@@ -434,14 +468,9 @@ decode_attention_step_kernel(const bf16* qkv, int nh, int nkv, int hd, const bf1
   pdl_prologue();
   constexpr int nw = kFaThreads / 32;
   constexpr int per_warp = kFaChunk / nw;
-  extern __shared__ float sh[];      // q, k_new, v_new, tmp (hd each), scores (kFaChunk), po (nw x hd), 33
-  float* qf = sh;
-  float* kn = qf + hd;
-  float* vn = kn + hd;
-  float* tmp = vn + hd;
-  float* sc = tmp + hd;
+  extern __shared__ float sh[];      // scores (kFaChunk), per-warp partial rows (nw x hd)
+  float* sc = sh;
   float* po = sc + kFaChunk;
-  float* red = po + nw * hd;
   __shared__ int s_last;
   const int head = blockIdx.x, row = blockIdx.y, split = blockIdx.z, rows = gridDim.y;
   const int group = nh / nkv, kvh = head / group;
@@ -471,69 +500,62 @@ decode_attention_step_kernel(const bf16* qkv, int nh, int nkv, int hd, const bf1
       kr[i] = ld ? *reinterpret_cast<const uint4*>(kbase + (int64_t)j * hd + lane * 8) : make_uint4(0, 0, 0, 0);
       vr[i] = ld ? *reinterpret_cast<const uint4*>(vbase + (int64_t)j * hd + lane * 8) : make_uint4(0, 0, 0, 0);
     }
-    fa_norm_rope(xrow + (int64_t)head * hd, qnw, eps, hd, cr, sr, tmp, red, qf);
+    // every warp normalises and rotates the query head itself (registers, no block barrier)
+    float q8[8];
+    fa_warp_norm_rope(xrow + (int64_t)head * hd, qnw, eps, hd, cr, sr, q8);
+    float kn8[8], vn8[8];
     const bool has_new = c1 == p + 1;
     if (has_new) {
-      fa_norm_rope(xrow + (int64_t)(nh + kvh) * hd, knw, eps, hd, cr, sr, tmp, red, kn);
+      fa_warp_norm_rope(xrow + (int64_t)(nh + kvh) * hd, knw, eps, hd, cr, sr, kn8);
       const bf16* vsrc = xrow + (int64_t)(nh + nkv + kvh) * hd;
-      for (int d = threadIdx.x; d < hd; d += blockDim.x) vn[d] = ldb(vsrc + d);
-      if (head % group == 0) {
-        for (int d = threadIdx.x; d < hd; d += blockDim.x) {
-          kbase[(int64_t)p * hd + d] = __float2bfloat16_rn(kn[d]);
-          vbase[(int64_t)p * hd + d] = vsrc[d];
-        }
+      uint4 vraw = make_uint4(0, 0, 0, 0);
+      if (act) vraw = *reinterpret_cast<const uint4*>(vsrc + lane * 8);
+      unpack8(vraw, vn8);
+      if (head % group == 0 && warp == 0 && act) {   // the cache append, once per KV head
+        store8(kbase + (int64_t)p * hd + lane * 8, kn8);
+        *reinterpret_cast<uint4*>(vbase + (int64_t)p * hd + lane * 8) = vraw;
       }
-      __syncthreads();
     }
-    float q8[8];
-#pragma unroll
-    for (int i = 0; i < 8; ++i) q8[i] = act ? qf[lane * 8 + i] : 0.f;
 #pragma unroll
     for (int i = 0; i < per_warp; ++i) {
       const int j = c0 + warp + nw * i;
       float kv[8];
       if (j == p) {
 #pragma unroll
-        for (int e = 0; e < 8; ++e) kv[e] = act ? kn[lane * 8 + e] : 0.f;
+        for (int e = 0; e < 8; ++e) kv[e] = kn8[e];
       } else {
         unpack8(kr[i], kv);
       }
       float acc = 0.f;
 #pragma unroll
       for (int e = 0; e < 8; ++e) acc += q8[e] * kv[e];
-#pragma unroll
-      for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+      acc = warp_sum(acc);
       if (lane == 0 && j < c1) sc[j - c0] = acc * scaling;
     }
     __syncthreads();
+    // every warp: max and sum of the range's (at most 64) scores, two per lane
     const int n = c1 - c0;
-    float m = -INFINITY;
-    for (int j = threadIdx.x; j < n; j += blockDim.x) m = fmaxf(m, sc[j]);
-    m = block_max(m, red);
-    float ssum = 0.f;
-    for (int j = threadIdx.x; j < n; j += blockDim.x) {
-      const float e = __expf(sc[j] - m);
-      sc[j] = e;
-      ssum += e;
-    }
-    const float l = block_sum(ssum, red);        // ends with a barrier: every sc[j] is final
+    const float s0 = lane < n ? sc[lane] : -INFINITY;
+    const float s1 = lane + 32 < n ? sc[lane + 32] : -INFINITY;
+    const float m = warp_max(fmaxf(s0, s1));
+    const float l = warp_sum((lane < n ? __expf(s0 - m) : 0.f) + (lane + 32 < n ? __expf(s1 - m) : 0.f));
     float o8[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-    if (act) {
 #pragma unroll
-      for (int i = 0; i < per_warp; ++i) {
-        const int j = c0 + warp + nw * i;
-        if (j >= c1) continue;
-        float vv[8];
-        if (j == p) {
+    for (int i = 0; i < per_warp; ++i) {
+      const int j = c0 + warp + nw * i;
+      if (j >= c1) continue;
+      float vv[8];
+      if (j == p) {
 #pragma unroll
-          for (int e = 0; e < 8; ++e) vv[e] = vn[lane * 8 + e];
-        } else {
-          unpack8(vr[i], vv);
-        }
-        const float pj = sc[j - c0];
-#pragma unroll
-        for (int e = 0; e < 8; ++e) o8[e] += pj * vv[e];
+        for (int e = 0; e < 8; ++e) vv[e] = vn8[e];
+      } else {
+        unpack8(vr[i], vv);
       }
+      const float pj = __expf(sc[j - c0] - m);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) o8[e] += pj * vv[e];
+    }
+    if (act) {
 #pragma unroll
       for (int e = 0; e < 8; ++e) po[warp * hd + lane * 8 + e] = o8[e];
     }
@@ -744,8 +766,8 @@ extern "C" int fbfp_decode_attention_step(const void* qkv, int64_t b, int64_t nh
   FBFP_CHECK_ARG(qkv && q_norm_w && k_norm_w && cos_table && sin_table && pos && k_cache && v_cache && scratch &&
                      out && err,
                  "null pointer");
-  FBFP_CHECK_ARG(nh > 0 && nkv > 0 && nh % nkv == 0 && hd > 0 && hd <= 256 && hd % 8 == 0,
-                 "bad head shape (nh %lld, nkv %lld, hd %lld: hd a multiple of 8 up to 256)", (long long)nh,
+  FBFP_CHECK_ARG(nh > 0 && nkv > 0 && nh % nkv == 0 && hd > 0 && hd <= 256 && hd % 16 == 0,
+                 "bad head shape (nh %lld, nkv %lld, hd %lld: hd a multiple of 16 up to 256)", (long long)nh,
                  (long long)nkv, (long long)hd);
   FBFP_CHECK_ARG(b >= 1 && b <= 65535 && max_ctx > 0 && max_ctx < (1 << 30), "bad batch %lld or max_ctx %lld",
                  (long long)b, (long long)max_ctx);
@@ -758,7 +780,7 @@ extern "C" int fbfp_decode_attention_step(const void* qkv, int64_t b, int64_t nh
   FBFP_CHECK_ARG(splits <= 65535, "max_ctx too large");
   int* counters = reinterpret_cast<int*>(scratch);
   float* part = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(scratch) + (nh * b * 4 + 255) / 256 * 256);
-  const size_t smem = sizeof(float) * (4 * (size_t)hd + kFaChunk + (kFaThreads / 32) * (size_t)hd + 33);
+  const size_t smem = sizeof(float) * (kFaChunk + (kFaThreads / 32) * (size_t)hd);
   FBFP_CUDA_TRY(launch_pdl(decode_attention_step_kernel, dim3((unsigned)nh, (unsigned)b, (unsigned)splits),
                            dim3(kFaThreads), smem, as_stream(stream), reinterpret_cast<const bf16*>(qkv), (int)nh,
                            (int)nkv, (int)hd, reinterpret_cast<const bf16*>(q_norm_w),

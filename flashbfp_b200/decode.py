@@ -102,8 +102,8 @@ class GemmaDecoder:
         self.rank = reducer.rank if reducer is not None else 0
         if len(layers) != len(s.layer_types):
             raise ValueError(f"{len(layers)} layers but {len(s.layer_types)} layer types")
-        if s.head_dim % 8 or s.head_dim > 256 or max_ctx + 8 * s.head_dim > 10000:
-            raise ValueError("head_dim must be a multiple of 8 up to 256, and max_ctx + 8 * head_dim "
+        if s.head_dim % 16 or s.head_dim > 256 or max_ctx + 8 * s.head_dim > 10000:
+            raise ValueError("head_dim must be a multiple of 16 up to 256, and max_ctx + 8 * head_dim "
                              "at most 10000")
         if s.n_heads % self.world or s.n_kv_heads % self.world:
             raise ValueError(f"heads ({s.n_heads} / {s.n_kv_heads}) do not split over {self.world} ranks")

@@ -314,7 +314,8 @@ int fbfp_compress_outliers(const void* w, int w_dtype, int64_t n_out, int64_t k_
  * fbfp_decode_attention_step: fbfp_qk_rope_cache followed by fbfp_decode_attention for such rows
  *   in one launch (the q/k norm, rotation and cache append folded into the attention, which is
  *   split over positions in ranges of 64 and merged by the last CTA of each head and row); out
- *   [b][nh][hd]. `scratch`: fbfp_decode_attention_step_scratch_bytes(b, nh, hd, max_ctx) bytes,
+ *   [b][nh][hd] (hd a multiple of 16 up to 256). `scratch`:
+ *   fbfp_decode_attention_step_scratch_bytes(b, nh, hd, max_ctx) bytes,
  *   16-byte aligned and zeroed once before the first call (every call leaves its counters at
  *   zero). A position outside [0, max_ctx) sets *err = 2 and skips that row.
  * fbfp_advance_positions: pos[r] += 1 for r < b (1 <= b <= 1024).
