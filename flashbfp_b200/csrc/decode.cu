@@ -480,10 +480,15 @@ decode_attention_step_kernel(const bf16* qkv, int nh, int nkv, int hd, const bf1
     return;
   }
   const int lo = (window > 0 && p - window + 1 > 0) ? p - window + 1 : 0;
+  // the ranges that hold positions of the row's window: the others have nothing to do and are
+  // not counted; a row with one such range writes its output without a merge
+  const int s_lo = lo / kFaChunk, s_hi = p / kFaChunk;
+  if (split < s_lo || split > s_hi) return;
+  const bool single = s_lo == s_hi;
   const int c0 = max(lo, split * kFaChunk), c1 = min(p + 1, (split + 1) * kFaChunk);
   float* mine = part + (((int64_t)head * rows + row) * n_splits + split) * (hd + 2);
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  if (c0 < c1) {
+  {
     const bf16* xrow = qkv + (int64_t)row * (nh + 2 * nkv) * hd;
     const bf16* cr = cos_t + (int64_t)p * hd;
     const bf16* sr = sin_t + (int64_t)p * hd;
@@ -560,44 +565,39 @@ decode_attention_step_kernel(const bf16* qkv, int nh, int nkv, int hd, const bf1
       for (int e = 0; e < 8; ++e) po[warp * hd + lane * 8 + e] = o8[e];
     }
     __syncthreads();
+    bf16* orow = out + ((int64_t)row * nh + head) * hd;
     for (int d = threadIdx.x; d < hd; d += blockDim.x) {
       float acc = 0.f;
 #pragma unroll
       for (int w = 0; w < nw; ++w) acc += po[w * hd + d];
-      mine[2 + d] = acc;
+      if (single) orow[d] = __float2bfloat16_rn(acc * (1.f / l));
+      else mine[2 + d] = acc;
     }
+    if (single) return;
     if (threadIdx.x == 0) { mine[0] = m; mine[1] = l; }
-  } else if (threadIdx.x == 0) {                 // no position of the window in this range
-    mine[0] = -INFINITY;
-    mine[1] = 0.f;
   }
-  // the last CTA of (head, row) merges the partials
+  // the last CTA of (head, row) merges the partials of ranges s_lo .. s_hi
   __threadfence();
   __syncthreads();
-  if (threadIdx.x == 0) s_last = atomicAdd(counters + head * rows + row, 1) == n_splits - 1;
+  if (threadIdx.x == 0) s_last = atomicAdd(counters + head * rows + row, 1) == s_hi - s_lo;
   __syncthreads();
   if (!s_last) return;
   __threadfence();
   const float* base = part + ((int64_t)head * rows + row) * n_splits * (hd + 2);
   float M = -INFINITY;
-  for (int s2 = 0; s2 < n_splits; ++s2) {
-    const float* ps = base + (int64_t)s2 * (hd + 2);
-    if (__ldcg(ps + 1) > 0.f) M = fmaxf(M, __ldcg(ps));
-  }
+  for (int s2 = s_lo; s2 <= s_hi; ++s2) M = fmaxf(M, __ldcg(base + (int64_t)s2 * (hd + 2)));
   float L = 0.f;
-  for (int s2 = 0; s2 < n_splits; ++s2) {
+  for (int s2 = s_lo; s2 <= s_hi; ++s2) {
     const float* ps = base + (int64_t)s2 * (hd + 2);
-    const float ls = __ldcg(ps + 1);
-    if (ls > 0.f) L += ls * __expf(__ldcg(ps) - M);
+    L += __ldcg(ps + 1) * __expf(__ldcg(ps) - M);
   }
   const float inv = 1.f / L;
   bf16* orow = out + ((int64_t)row * nh + head) * hd;
   for (int d = threadIdx.x; d < hd; d += blockDim.x) {
     float acc = 0.f;
-    for (int s2 = 0; s2 < n_splits; ++s2) {
+    for (int s2 = s_lo; s2 <= s_hi; ++s2) {
       const float* ps = base + (int64_t)s2 * (hd + 2);
-      const float ls = __ldcg(ps + 1);
-      if (ls > 0.f) acc += __ldcg(ps + 2 + d) * __expf(__ldcg(ps) - M);
+      acc += __ldcg(ps + 2 + d) * __expf(__ldcg(ps) - M);
     }
     orow[d] = __float2bfloat16_rn(acc * inv);
   }
