@@ -711,7 +711,7 @@ constexpr int kConsumers = 16;
 constexpr int kThreads = 32 * (2 + kConsumers);       // 576
 constexpr int kNW = 6;
 constexpr int kNX = 8;
-constexpr int kXSlot = 1152;                          // 256 fp32 activations + 16 block sums
+constexpr int kXSlot = 1152;                          // 256 bf16 activations, 16 fp32 block sums at byte 512
 constexpr size_t kXOff = (size_t)kNW * rec::kStageBytes;
 constexpr size_t kRedOff = kXOff + (size_t)kNX * kXSlot;          // [2][4][128] fp32 row sums
 constexpr size_t kOffOff = kRedOff + 2 * 4 * 128 * sizeof(float);
@@ -721,53 +721,54 @@ constexpr size_t kSmemBytes = kBarOff + kNumBars * 8 + 16 + 1024;
 static_assert(kSmemBytes <= 232448, "shared memory budget");
 }  // namespace cc
 
-// acc(x2) += v(x2) * x(x2) on packed fp32 pairs held in 64-bit registers.
-__device__ __forceinline__ void ffma2(uint64_t& acc, uint64_t v, uint64_t x) {
-  asm("fma.rn.f32x2 %0, %1, %2, %0;" : "+l"(acc) : "l"(v), "l"(x));
-}
-
-// Field of pair P's element (lo: bits 5 (P % 3), hi: bits 16 + 5 (P % 3) of its word) moved to
-// mantissa bits 18-22 and given the exponent bits E; the pair packed as {lo, hi}. Left shifts are
-// written as multiplications so that they may issue on the FMA pipe next to the ALU's LOP3s.
+// Field pair K of word w (bits 5K and 16 + 5K) as a bf16 pair (Kb | f): each element is
+// 2^e (128 + f), exactly (Kb = eb * 0x00800080 puts the biased exponent e + 134 in both halves).
 template <int K>
-__device__ __forceinline__ uint64_t cc_pair(uint32_t w, uint32_t E) {
-  const uint32_t lo = ((w * (1u << (18 - 5 * K))) & 0x007C0000u) | E;
-  const uint32_t t = K == 0 ? w * 4u : (w >> (5 * K - 2));
-  const uint32_t hi = (t & 0x007C0000u) | E;
-  return ((uint64_t)hi << 32) | lo;
+__device__ __forceinline__ uint32_t cc_bpair(uint32_t w, uint32_t Kb) {
+  return ((K == 0 ? w : (w >> (5 * K))) & 0x001F001Fu) | Kb;
 }
 
-// 32 * sum(v x) - 48 * 2^e * sum(x) of one block: its 8 pairs, x the block's 16 activations
-// (fp32), sx their sum, eb the biased exponent (e + 134).
-__device__ __forceinline__ float cc_block(const uint64_t (&v)[8], const float* x, float sx, uint32_t eb) {
-  uint64_t t = 0;                                   // two fp32 partial sums {even, odd elements}
-  const ulonglong2* x2 = reinterpret_cast<const ulonglong2*>(x);
-#pragma unroll
-  for (int j = 0; j < 4; ++j) {
-    const ulonglong2 xv = x2[j];
-    ffma2(t, v[2 * j], xv.x);
-    ffma2(t, v[2 * j + 1], xv.y);
-  }
-  const float c48 = __uint_as_float(((eb - 2u) << 23) | 0x00400000u);     // 1.5 * 2^(e + 5)
-  const float sum = __uint_as_float((uint32_t)t) + __uint_as_float((uint32_t)(t >> 32));
-  return fmaf(-c48, sx, 32.f * sum);
+// acc += b.lo * x.lo + b.hi * x.hi: bf16 operands, fp32 accumulation (mixed-precision FMA, one
+// rounding each, the products exact).
+__device__ __forceinline__ void fma_bf16x2(float& acc, uint32_t b, uint32_t x) {
+  asm("{ .reg .b16 bl, bh, xl, xh;\n"
+      "  mov.b32 {bl, bh}, %1;\n"
+      "  mov.b32 {xl, xh}, %2;\n"
+      "  fma.rn.f32.bf16 %0, bl, xl, %0;\n"
+      "  fma.rn.f32.bf16 %0, bh, xh, %0;\n"
+      "}" : "+f"(acc) : "r"(b), "r"(x));
 }
 
-// Blocks 2h, 2h+1 of a substage (five words, biased exponents eb0, eb1), x their 32 activations.
-__device__ __forceinline__ float cc_block_pair(uint32_t w0, uint32_t w1, uint32_t w2, uint32_t w3, uint32_t w4,
-                                               uint32_t eb0, uint32_t eb1, const float* x, float sx0, float sx1) {
-  const uint32_t E0 = (eb0 - 7u) << 23, E1 = (eb1 - 7u) << 23;
-  uint64_t v[8];
-  v[0] = cc_pair<0>(w0, E0); v[1] = cc_pair<1>(w0, E0); v[2] = cc_pair<2>(w0, E0);
-  v[3] = cc_pair<0>(w1, E0); v[4] = cc_pair<1>(w1, E0); v[5] = cc_pair<2>(w1, E0);
-  v[6] = cc_pair<0>(w2, E0); v[7] = cc_pair<1>(w2, E0);
-  float r = cc_block(v, x, sx0, eb0);
+// Blocks 2h, 2h+1 of a substage (five words, biased exponents eb0, eb1), x their 32 bf16
+// activations (16 pair words in 4 uint4), sx0 / sx1 the blocks' activation sums. Adds
+// sum(b x) = 2^e (144 sum(x) + sum(s m x)) over both blocks into acc0 / acc1 (even / odd pairs)
+// and 144 2^e sum(x) into corr, so that acc0 + acc1 - corr = sum of 2^e s m x.
+__device__ __forceinline__ void cc_block_pair(uint32_t w0, uint32_t w1, uint32_t w2, uint32_t w3, uint32_t w4,
+                                              uint32_t eb0, uint32_t eb1, const uint4* x4, float sx0, float sx1,
+                                              float& acc0, float& acc1, float& corr) {
+  const uint32_t K0 = eb0 * 0x00800080u, K1 = eb1 * 0x00800080u;
+  const uint4 xa = x4[0], xb = x4[1], xc = x4[2], xd = x4[3];
+  fma_bf16x2(acc0, cc_bpair<0>(w0, K0), xa.x);
+  fma_bf16x2(acc1, cc_bpair<1>(w0, K0), xa.y);
+  fma_bf16x2(acc0, cc_bpair<2>(w0, K0), xa.z);
+  fma_bf16x2(acc1, cc_bpair<0>(w1, K0), xa.w);
+  fma_bf16x2(acc0, cc_bpair<1>(w1, K0), xb.x);
+  fma_bf16x2(acc1, cc_bpair<2>(w1, K0), xb.y);
+  fma_bf16x2(acc0, cc_bpair<0>(w2, K0), xb.z);
+  fma_bf16x2(acc1, cc_bpair<1>(w2, K0), xb.w);
   const uint32_t t = ((w0 >> 15) & 0x00010001u) | ((w1 >> 14) & 0x00020002u) | ((w2 >> 13) & 0x00040004u) |
                      ((w3 >> 12) & 0x00080008u) | ((w4 >> 11) & 0x00100010u);
-  v[0] = cc_pair<2>(w2, E1); v[1] = cc_pair<0>(w3, E1); v[2] = cc_pair<1>(w3, E1);
-  v[3] = cc_pair<2>(w3, E1); v[4] = cc_pair<0>(w4, E1); v[5] = cc_pair<1>(w4, E1);
-  v[6] = cc_pair<2>(w4, E1); v[7] = cc_pair<0>(t, E1);
-  return r + cc_block(v, x + 16, sx1, eb1);
+  fma_bf16x2(acc0, cc_bpair<2>(w2, K1), xc.x);
+  fma_bf16x2(acc1, cc_bpair<0>(w3, K1), xc.y);
+  fma_bf16x2(acc0, cc_bpair<1>(w3, K1), xc.z);
+  fma_bf16x2(acc1, cc_bpair<2>(w3, K1), xc.w);
+  fma_bf16x2(acc0, cc_bpair<0>(w4, K1), xd.x);
+  fma_bf16x2(acc1, cc_bpair<1>(w4, K1), xd.y);
+  fma_bf16x2(acc0, cc_bpair<2>(w4, K1), xd.z);
+  fma_bf16x2(acc1, cc_bpair<0>(t, K1), xd.w);
+  // 144 * 2^e = 1.125 * 2^(e + 7): exponent field e + 134 = eb, mantissa 1/8
+  corr = fmaf(__uint_as_float((eb0 << 23) | 0x00100000u), sx0, corr);
+  corr = fmaf(__uint_as_float((eb1 << 23) | 0x00100000u), sx1, corr);
 }
 
 __device__ void cc_xproducer(const RecShared& S, const RecArgs& a, int64_t u0, int64_t u1) {
@@ -792,7 +793,7 @@ __device__ void cc_xproducer(const RecShared& S, const RecArgs& a, int64_t u0, i
       if (j >= nb) break;
       const int64_t i = i0 + j;
       const int s = (int)(i % cc::kNX);
-      float* xs = reinterpret_cast<float*>(S.xring + (size_t)s * cc::kXSlot);
+      uint8_t* xsl = S.xring + (size_t)s * cc::kXSlot;
       const uint32_t r[4] = {raw[j].x, raw[j].y, raw[j].z, raw[j].w};
       float f[8];
 #pragma unroll
@@ -800,11 +801,10 @@ __device__ void cc_xproducer(const RecShared& S, const RecArgs& a, int64_t u0, i
         f[2 * q] = __uint_as_float(r[q] << 16);
         f[2 * q + 1] = __uint_as_float(r[q] & 0xFFFF0000u);
       }
-      *reinterpret_cast<float4*>(xs + lane * 8) = make_float4(f[0], f[1], f[2], f[3]);
-      *reinterpret_cast<float4*>(xs + lane * 8 + 4) = make_float4(f[4], f[5], f[6], f[7]);
+      *reinterpret_cast<uint4*>(xsl + lane * 16) = raw[j];           // 256 bf16 activations
       float s8 = ((f[0] + f[1]) + (f[2] + f[3])) + ((f[4] + f[5]) + (f[6] + f[7]));
       s8 += __shfl_xor_sync(0xffffffffu, s8, 1);
-      if ((lane & 1) == 0) xs[256 + lane / 2] = s8;
+      if ((lane & 1) == 0) reinterpret_cast<float*>(xsl + 512)[lane / 2] = s8;   // 16 block sums
       __syncwarp();
       if (lane == 0) mbar_arrive(&S.full_x[s]);
     }
@@ -835,7 +835,7 @@ __device__ void cc_consumer(const RecShared& S, const RecArgs& a, int64_t u0, in
     const int64_t rg = u / a.n_stages;
     const int64_t seg_begin = u, seg_end = min(u1, (rg + 1) * a.n_stages);
     const int64_t row = rg * 128 + lr;
-    float acc = 0.f, oacc = 0.f;
+    float acc0 = 0.f, acc1 = 0.f, corr = 0.f, oacc = 0.f;
     for (; u < seg_end; ++u, ++i) {
       const int s = (int)(i % cc::kNW), sx = (int)(i % cc::kNX);
       if (alive) {
@@ -844,31 +844,42 @@ __device__ void cc_consumer(const RecShared& S, const RecArgs& a, int64_t u0, in
       }
       if (alive) {
         const uint8_t* rb = S.wring + (size_t)s * rec::kStageBytes;
-        const float* xf = reinterpret_cast<const float*>(S.xring + (size_t)sx * cc::kXSlot);
-        const float* xs = xf + 64 * c;
-        const float4 sx4 = *reinterpret_cast<const float4*>(xf + 256 + 4 * c);
+        const uint8_t* xsl = S.xring + (size_t)sx * cc::kXSlot;
+        const uint4* xs = reinterpret_cast<const uint4*>(xsl + 128 * c);     // 64 bf16 of the substage
+        const uint16_t* xh = reinterpret_cast<const uint16_t*>(xsl);
+        const float4 sx4 = *reinterpret_cast<const float4*>(xsl + 512 + 16 * c);
         const uint8_t* sb = rb + c * 5120;
         const uint4 A = *reinterpret_cast<const uint4*>(sb + lr * 16);
         const uint4 B = *reinterpret_cast<const uint4*>(sb + 2048 + lr * 16);
         const uint2 Cw = *reinterpret_cast<const uint2*>(sb + 4096 + lr * 8);
         const uint32_t EB = *reinterpret_cast<const uint32_t*>(rb + rec::kExpOff + c * 512 + lr * 4);
-        acc += cc_block_pair(A.x, A.y, A.z, A.w, B.x, EB & 0xFFu, (EB >> 8) & 0xFFu, xs, sx4.x, sx4.y);
-        acc += cc_block_pair(B.y, B.z, B.w, Cw.x, Cw.y, (EB >> 16) & 0xFFu, EB >> 24, xs + 32, sx4.z, sx4.w);
+        cc_block_pair(A.x, A.y, A.z, A.w, B.x, EB & 0xFFu, (EB >> 8) & 0xFFu, xs, sx4.x, sx4.y, acc0, acc1, corr);
+        cc_block_pair(B.y, B.z, B.w, Cw.x, Cw.y, (EB >> 16) & 0xFFu, EB >> 24, xs + 4, sx4.z, sx4.w, acc0, acc1,
+                      corr);
         if (a.outliers) {                     // every fourth of the row's entries
           const uint16_t* ro = reinterpret_cast<const uint16_t*>(rb + rec::kRoffOff);
           const uint32_t* es = reinterpret_cast<const uint32_t*>(rb + rec::kEntOff);
-          const uint32_t* gs = reinterpret_cast<const uint32_t*>(a.rec + rec_offset(S, a, u0, i) + rec::kEntOff);
           const int k1 = ro[lr + 1];
-          for (int k = ro[lr] + c; k < k1; k += 16) {     // four of this warp's entries per step
-            uint32_t e[4];
+          for (int k = ro[lr] + c; k < k1; k += 8) {      // two of this warp's entries per step
+            uint32_t e[2];
 #pragma unroll
-            for (int j = 0; j < 4; ++j) {
+            for (int j = 0; j < 2; ++j) {
               const int kk = k + 4 * j;
-              e[j] = kk < k1 ? (kk < rec::kOutCap ? es[kk] : __ldg(gs + kk)) : 0u;
+              e[j] = 0u;
+              if (kk < k1) {
+                if (kk < rec::kOutCap) {
+                  e[j] = es[kk];
+                } else {                      // beyond the staged entries: from the record
+                  const uint32_t* gs =
+                      reinterpret_cast<const uint32_t*>(a.rec + rec_offset(S, a, u0, i) + rec::kEntOff);
+                  e[j] = __ldg(gs + kk);
+                }
+              }
             }
 #pragma unroll
-            for (int j = 0; j < 4; ++j)
-              oacc = fmaf(__half2float(__ushort_as_half((unsigned short)(e[j] & 0xFFFFu))), xf[(e[j] >> 16) & 0xFFu], oacc);
+            for (int j = 0; j < 2; ++j)
+              oacc = fmaf(__half2float(__ushort_as_half((unsigned short)(e[j] & 0xFFFFu))),
+                          __uint_as_float((uint32_t)xh[(e[j] >> 16) & 0xFFu] << 16), oacc);
           }
         }
       }
@@ -878,7 +889,7 @@ __device__ void cc_consumer(const RecShared& S, const RecArgs& a, int64_t u0, in
     // the four substage warps of this lane quarter add their row sums in a fixed order (every
     // consumer warp reaches this barrier once per segment, also after a wait gave up)
     float* rbuf = red + (seg & 1) * (4 * 128);
-    rbuf[c * 128 + lr] = fmaf(acc, inv15, oacc);
+    rbuf[c * 128 + lr] = fmaf((acc0 + acc1) - corr, inv15, oacc);
     cc_named_sync();
     if (c != 0) continue;
     float val[1] = {((rbuf[lr] + rbuf[128 + lr]) + rbuf[256 + lr]) + rbuf[384 + lr]};
