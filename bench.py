@@ -135,9 +135,12 @@ def _progress(rank, msg):
 GEMMA12B = dict(n_heads=16, n_kv_heads=8, head_dim=256, inter=15360, vocab=262144, hidden=3840)
 
 
-def build_layers(n_layers, rank, world, device, shapes=None, plan_args=None, frac=0.015, seed0=1000):
+def build_layers(n_layers, rank, world, device, shapes=None, plan_args=None, frac=0.015, seed0=1000,
+                 records=True):
     """Every linear of n_layers decoder layers, this rank's part as the whole-model tensor-parallel
-    plan splits it (whole heads; the MLP in 256-column stages), compressed on the GPU."""
+    plan splits it (whole heads; the MLP in 256-column stages), compressed on the GPU; with
+    ``records`` also the stage records that one-token launches read (about the packed size again
+    in device memory)."""
     from flashbfp_b200 import OABFCompressor, packed, tp, workloads
     comp = OABFCompressor(16, 64)
     shapes = shapes or workloads.GEMMA12B_LAYER
@@ -162,6 +165,8 @@ def build_layers(n_layers, rank, world, device, shapes=None, plan_args=None, fra
         }
         for kk in KINDS:
             shard_bytes[kk] += L[kk].packed_bytes()
+            if records:
+                L[kk].build_records()
         layers.append(L)
         if li % 8 == 7:
             torch.cuda.empty_cache()
@@ -409,7 +414,7 @@ def run_ours(args):
             "decode_tokens_per_s_note": "linear layers only (no attention/norm/lm_head)",
             "layers_gbs_per_rank": {kk: round(v, 1) for kk, v in per_rank_kind.items()},
             "roofline": {
-                "bound": "hbm", "kernel": "gemv_tc_kernel (gate|up 30720x3840 launches)",
+                "bound": "hbm", "kernel": "gemv_cc_kernel (stage records, gate|up 30720x3840 launches)",
                 "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                 "frac": round(achieved / peak, 4), "peak_source": peaks["source"],
                 "traffic": _traffic(m),
@@ -445,6 +450,10 @@ def run_ours(args):
 
 
 def _gemv(L, _lib, X, pw, Y, ws):
+    from flashbfp_b200.linear import gemv_records, records_eligible
+    if X.shape[0] == 1 and records_eligible(X, pw):     # one token: the stage-record kernel
+        gemv_records(X, pw, Y, ws)
+        return
     gemv = L.fbfp_gemv_resident if pw.resident else L.fbfp_gemv
     _lib.check(gemv(_lib.ptr(X), _lib.DTYPE_CODE[X.dtype], X.shape[0], X.stride(0),
                            _lib.ptr(pw.exps), _lib.ptr(pw.signs), _lib.ptr(pw.payload), pw.n_out,
@@ -455,6 +464,10 @@ def _gemv(L, _lib, X, pw, Y, ws):
 
 
 def _gemv_fused(L, _lib, X, pw, Y, ws, reducer):
+    from flashbfp_b200.linear import gemv_records, records_eligible
+    if X.shape[0] == 1 and records_eligible(X, pw):
+        gemv_records(X, pw, Y, ws, reducer=reducer)
+        return
     _lib.check(L.fbfp_gemv_allreduce(_lib.ptr(X), _lib.DTYPE_CODE[X.dtype], X.shape[0], X.stride(0),
                                      _lib.ptr(pw.exps), _lib.ptr(pw.signs), _lib.ptr(pw.payload), pw.n_out,
                                      pw.k_in, pw.kpad, pw.npad, _lib.ptr(pw.entries if pw.nnz else None),

@@ -60,7 +60,8 @@ GEMV_RESIDENT, GEMV_DENSE_ONLY, GEMV_TENSOR_CORES = 1, 4, 8
 
 
 def records_eligible(X: torch.Tensor, pw: PackedWeight) -> bool:
-    """Whether the stage-record GEMV takes X (at most 16 tokens per launch) on pw."""
+    """Whether the stage-record GEMV takes X (at most 16 tokens per launch) on pw (its records
+    built by ``PackedWeight.build_records``). ``packed_linear`` sends it one-token launches."""
     return (pw.records is not None and X.dtype == torch.bfloat16 and X.stride(1) == 1
             and X.stride(0) % 8 == 0 and X.data_ptr() % 16 == 0 and pw.k_in % 8 == 0)
 
@@ -122,10 +123,10 @@ def packed_linear(X: torch.Tensor, pw: PackedWeight, bias: torch.Tensor | None =
                                        _lib.ptr(bias), bd, _lib.ptr(Y), yd, Y.stride(0), _lib.ptr(ws), st),
                    "fbfp_gemm_prefill")
         return Y
-    if records_eligible(X, pw):
-        for m0 in range(0, M, 16):
-            m = min(16, M - m0)
-            gemv_records(X[m0:m0 + m], pw, Y[m0:m0 + m], ws, bias, with_outliers)
+    if M == 1 and records_eligible(X, pw):
+        # one token: the stage-record kernel on the CUDA cores (faster than the tcgen05 GEMV
+        # at one token; from two tokens on, the tcgen05 GEMV below is the faster one)
+        gemv_records(X, pw, Y, ws, bias, with_outliers)
         return Y
     gemv = L.fbfp_gemv_resident if pw.resident else L.fbfp_gemv
     for m0 in range(0, M, 16):
@@ -174,10 +175,8 @@ def packed_linear_allreduce(X: torch.Tensor, pw: PackedWeight, reducer, bias: to
     yd = _lib.dtype_code(out_dtype, "Y")
     ws = gemv_workspace(X.device, pw.npad)
     st = _lib.stream_ptr(X.device)
-    if records_eligible(X, pw):
-        for m0 in range(0, M, 16):
-            m = min(16, M - m0)
-            gemv_records(X[m0:m0 + m], pw, Y[m0:m0 + m], ws, bias, True, reducer)
+    if M == 1 and records_eligible(X, pw):
+        gemv_records(X, pw, Y, ws, bias, True, reducer)
         return Y
     for m0 in range(0, M, 16):
         m = min(16, M - m0)
