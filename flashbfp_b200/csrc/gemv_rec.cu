@@ -830,17 +830,18 @@ __device__ void cc_consumer(const RecShared& S, const RecArgs& a, int64_t u0, in
     tag = e + 1u;
   }
   int64_t seg = 0, i = 0;
+  int s = 0, sx = 0;                          // ring slots of unit i and their phases
+  uint32_t ph = 0, phx = 0;
   bool alive = true;
   for (int64_t u = u0; u < u1; ++seg) {
     const int64_t rg = u / a.n_stages;
     const int64_t seg_begin = u, seg_end = min(u1, (rg + 1) * a.n_stages);
     const int64_t row = rg * 128 + lr;
-    float acc0 = 0.f, acc1 = 0.f, corr = 0.f, oacc = 0.f;
+    float acc0 = 0.f, acc1 = 0.f, acc2 = 0.f, acc3 = 0.f, corr = 0.f, oacc = 0.f;
     for (; u < seg_end; ++u, ++i) {
-      const int s = (int)(i % cc::kNW), sx = (int)(i % cc::kNX);
       if (alive) {
-        alive = __all_sync(0xffffffffu, rec_wait(S, a, &S.full_w[s], (uint32_t)(i / cc::kNW) & 1, 5)) &&
-                __all_sync(0xffffffffu, rec_wait(S, a, &S.full_x[sx], (uint32_t)(i / cc::kNX) & 1, 9));
+        alive = __all_sync(0xffffffffu, rec_wait(S, a, &S.full_w[s], ph, 5)) &&
+                __all_sync(0xffffffffu, rec_wait(S, a, &S.full_x[sx], phx, 9));
       }
       if (alive) {
         const uint8_t* rb = S.wring + (size_t)s * rec::kStageBytes;
@@ -854,7 +855,7 @@ __device__ void cc_consumer(const RecShared& S, const RecArgs& a, int64_t u0, in
         const uint2 Cw = *reinterpret_cast<const uint2*>(sb + 4096 + lr * 8);
         const uint32_t EB = *reinterpret_cast<const uint32_t*>(rb + rec::kExpOff + c * 512 + lr * 4);
         cc_block_pair(A.x, A.y, A.z, A.w, B.x, EB & 0xFFu, (EB >> 8) & 0xFFu, xs, sx4.x, sx4.y, acc0, acc1, corr);
-        cc_block_pair(B.y, B.z, B.w, Cw.x, Cw.y, (EB >> 16) & 0xFFu, EB >> 24, xs + 4, sx4.z, sx4.w, acc0, acc1,
+        cc_block_pair(B.y, B.z, B.w, Cw.x, Cw.y, (EB >> 16) & 0xFFu, EB >> 24, xs + 4, sx4.z, sx4.w, acc2, acc3,
                       corr);
         if (a.outliers) {                     // every fourth of the row's entries
           const uint16_t* ro = reinterpret_cast<const uint16_t*>(rb + rec::kRoffOff);
@@ -885,11 +886,13 @@ __device__ void cc_consumer(const RecShared& S, const RecArgs& a, int64_t u0, in
       }
       __syncwarp();
       if (lane == 0 && alive) { mbar_arrive(&S.empty_w[s]); mbar_arrive(&S.empty_x[sx]); }
+      if (++s == cc::kNW) { s = 0; ph ^= 1u; }
+      if (++sx == cc::kNX) { sx = 0; phx ^= 1u; }
     }
     // the four substage warps of this lane quarter add their row sums in a fixed order (every
     // consumer warp reaches this barrier once per segment, also after a wait gave up)
     float* rbuf = red + (seg & 1) * (4 * 128);
-    rbuf[c * 128 + lr] = fmaf((acc0 + acc1) - corr, inv15, oacc);
+    rbuf[c * 128 + lr] = fmaf(((acc0 + acc1) + (acc2 + acc3)) - corr, inv15, oacc);
     cc_named_sync();
     if (c != 0) continue;
     float val[1] = {((rbuf[lr] + rbuf[128 + lr]) + rbuf[256 + lr]) + rbuf[384 + lr]};
