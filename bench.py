@@ -21,7 +21,8 @@ the roofline kernel. ``e2e`` runs the same step through the public ``OABFLinear`
 the activations copied from pinned host memory each step and the outputs copied back. At N = 1
 the line also carries ``model_decode`` (whole tokens of a random-init 12B-class Gemma-3 around
 these linears: embedding, norms, RoPE, KV cache, attention, GeGLU, bf16 lm_head and the greedy
-pick in one CUDA graph per token), ``prefill`` (the gate|up linear at M = 2048 on the tcgen05
+pick in one CUDA graph per token), ``prefill`` (the gate|up linear at M = 2048 on the path
+packed_linear takes there, the two-pass expansion + cuBLASLt GEMM, beside the fused tcgen05
 prefill GEMM), ``bf16_cublas_decode`` and ``compress``.
 """
 from __future__ import annotations
@@ -553,11 +554,15 @@ def run_e2e(args, layers, xs, stream, device, world, rank, step_bytes, exchange,
 
 
 def run_prefill(layers, device, ms=(512, 2048, 8192), iters=5):
-    """Prefill GEMM (tensor-bound): the gate|up (30720x3840) and down (3840x15360) linears of
-    layer 0 at M bf16 tokens through packed_linear (fbfp_gemm_prefill), beside cuBLAS bf16 on a
-    dense bf16 weight of the same shape. CUDA events on the launching stream; 3 warm-up launches."""
+    """Prefill (tensor-bound): the gate|up (30720x3840) and down (3840x15360) linears of layer 0
+    at M bf16 tokens through packed_linear, on both paths: the fused tcgen05 kernel
+    (fbfp_gemm_prefill) and the two-pass one (fbfp_gemm_expanded: expansion of the packed matrix
+    into a bf16 scratch, then a cuBLASLt bf16 GEMM), which packed_linear takes where
+    ``expanded_preferred`` says so (512 tokens, or 256 when the fused kernel would have fewer tiles
+    than SMs); beside cuBLAS bf16 on a dense bf16 weight of the same shape. CUDA events on the
+    launching stream; 3 warm-up launches."""
     from flashbfp_b200 import workloads
-    from flashbfp_b200.linear import packed_linear, check_device_errors
+    from flashbfp_b200.linear import EXPANDED_MIN_M, expanded_preferred, packed_linear, check_device_errors
     peaks = _peaks()
 
     def timed(fn):
@@ -580,21 +585,30 @@ def run_prefill(layers, device, ms=(512, 2048, 8192), iters=5):
             X = workloads.activations(m, pw.k_in, seed=11, device=device)
             Y = torch.empty(m, pw.n_out, dtype=torch.bfloat16, device=device)
             flops = 2.0 * m * pw.n_out * pw.k_in
-            ms_ = timed(lambda: packed_linear(X, pw, out=Y))
+            ms_f = timed(lambda: packed_linear(X, pw, out=Y, prefill="fused"))
+            ms_e = timed(lambda: packed_linear(X, pw, out=Y, prefill="expanded"))
             check_device_errors(device)
             ms_b = timed(lambda: torch.matmul(X, Wb.t()))
+            path = "expanded" if expanded_preferred(m, pw, device) else "fused"
+            ms_ = ms_e if path == "expanded" else ms_f
             tf = flops / (ms_ * 1e-3) / 1e12
-            rows.append({"linear": f"{kk} {pw.n_out}x{pw.k_in}", "m": m, "ms": round(ms_, 4),
+            rows.append({"linear": f"{kk} {pw.n_out}x{pw.k_in}", "m": m, "path": path, "ms": round(ms_, 4),
                          "tflops": round(tf, 1), "frac": round(tf / peaks["bf16_tflops"], 4),
+                         "fused_tflops": round(flops / (ms_f * 1e-3) / 1e12, 1),
+                         "expanded_tflops": round(flops / (ms_e * 1e-3) / 1e12, 1),
                          "cublas_bf16_tflops": round(flops / (ms_b * 1e-3) / 1e12, 1)})
             del X, Y
         del Wb
     head = next(r for r in rows if r["m"] == 2048 and r["linear"].startswith("gate_up"))
+    fused_frac = round(head["fused_tflops"] / peaks["bf16_tflops"], 4)
     return {"workload": "prefill: OABF gate|up and down linears at M = 512, 2048, 8192 bf16 tokens",
-            "m": 2048, "ms": head["ms"], "tflops": head["tflops"],
+            "m": 2048, "path": head["path"], "ms": head["ms"], "tflops": head["tflops"],
             "roofline": {"bound": "tensor", "achieved": head["tflops"], "peak": peaks["bf16_tflops"],
                          "unit": "TFLOP/s", "frac": head["frac"], "peak_source": peaks["source"],
-                         "kernel": "prefill_tc_kernel (gate|up at M=2048)"},
+                         "kernel": f"{head['path']} path, gate|up at M=2048 (expanded: expand_x15_kernel "
+                                   "+ cuBLASLt bf16 GEMM; fused: prefill_tc_kernel)"},
+            "fused": {"kernel": "prefill_tc_kernel", "tflops": head["fused_tflops"], "frac": fused_frac},
+            "expanded_min_m": EXPANDED_MIN_M,
             "cublas_bf16_tflops": head["cublas_bf16_tflops"],
             "cublas_bf16_note": "torch.matmul on a dense bf16 weight of the same shape (uncompressed)",
             "sizes": rows}
@@ -898,7 +912,7 @@ def run_stress70b(device, rank, world, steps=10):
             check_device_errors(device)
             t = a.elapsed_time(c) / 3
             tf = 2.0 * 4096 * pw.n_out * pw.k_in / (t * 1e-3) / 1e12
-            pf.append({"linear": f"{kk} {pw.n_out}x{pw.k_in}", "m": 4096, "ms": round(t, 3),
+            pf.append({"linear": f"{kk} {pw.n_out}x{pw.k_in}", "m": 4096, "path": "expanded", "ms": round(t, 3),
                        "tflops": round(tf, 1), "frac": round(tf / _peaks()["bf16_tflops"], 4)})
             del X, Y
         out["prefill_m4096"] = pf

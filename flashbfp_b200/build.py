@@ -47,7 +47,8 @@ def build(force: bool = False, verbose: bool = False) -> str:
         subprocess.run(cmd, check=True)
         objs.append(obj)
     tmp = LIB + ".tmp"
-    cmd = [NVCC, *ARCH, "-shared", "-o", tmp, *objs]
+    cmd = [NVCC, *ARCH, "-shared", "-o", tmp, *objs, "-lcublasLt", "-Xlinker",
+           "-rpath=" + os.path.join(os.path.dirname(os.path.dirname(NVCC)), "lib64")]
     if verbose:
         print(" ".join(cmd), flush=True)
     subprocess.run(cmd, check=True)

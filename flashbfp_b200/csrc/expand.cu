@@ -1,0 +1,205 @@
+// expand.cu — two-pass prefill for many tokens: the packed matrix is expanded once into a bf16
+// scratch holding 15 x the dequantised weights, and a cuBLASLt bf16 GEMM (fp32 accumulation)
+// multiplies it with the activations, scaled back by 1/15, with the bias added in its epilogue.
+//
+// The scratch holds exactly the A operand the fused prefill kernel (gemm_tc.cu) builds in tensor
+// memory: dense elements s * m * 2^e (exact in bf16: m has at most four significant bits and
+// 2^e with e in [-126, 127] is a normal power of two) and outliers bf16(15 v) in their (+0)
+// slots, so the product matches the fused kernel's up to the order of the fp32 additions, and
+// the reference's (flash_bfp/triton_kernel.py:22-86 dequantises w = s * fl(m / 15) * 2^e to the
+// activation dtype, then multiplies) up to that one rounding.
+#include <cublasLt.h>
+
+#include "common.cuh"
+
+namespace fbfp {
+
+// One thread per 16-weight block: 11 packed bytes in, 32 bytes out (two 16-byte stores when the
+// block lies inside k_in, else element by element).
+__global__ void expand_x15_kernel(const int8_t* __restrict__ ex, const int16_t* __restrict__ sg,
+                                  const uint2* __restrict__ pay, int64_t n_out, int64_t k_in,
+                                  int64_t kb_row, int64_t kb_used, uint16_t* __restrict__ out,
+                                  int64_t ldo) {
+  const int64_t total = n_out * kb_used;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t n = i / kb_used, kb = i - n * kb_used;
+    const int64_t b = n * kb_row + kb;
+    const uint2 w = pay[b];
+    const uint32_t s = (uint16_t)sg[b];
+    const uint32_t ebits = (uint32_t)((int)ex[b] + 127) << 23;        // 2^e as fp32 bits
+    const float scale = __uint_as_float(ebits);
+    uint32_t h[16];
+#pragma unroll
+    for (int j = 0; j < 16; ++j) {
+      const uint32_t word = j < 8 ? w.x : w.y;
+      const uint32_t m = (word >> (4 * (j & 7))) & 0xFu;
+      // m * 2^e is exact in fp32 with zero low 16 bits, so its top half is the bf16 value
+      const uint32_t f = __float_as_uint((float)m * scale) | (((s >> j) & 1u) << 31);
+      h[j] = f >> 16;
+    }
+    const int64_t k0 = kb * kBlock;
+    uint16_t* dst = out + n * ldo + k0;
+    if (k0 + kBlock <= k_in) {
+      uint4 v0, v1;
+      v0.x = h[0] | (h[1] << 16);  v0.y = h[2] | (h[3] << 16);
+      v0.z = h[4] | (h[5] << 16);  v0.w = h[6] | (h[7] << 16);
+      v1.x = h[8] | (h[9] << 16);  v1.y = h[10] | (h[11] << 16);
+      v1.z = h[12] | (h[13] << 16); v1.w = h[14] | (h[15] << 16);
+      reinterpret_cast<uint4*>(dst)[0] = v0;
+      reinterpret_cast<uint4*>(dst)[1] = v1;
+    } else {
+#pragma unroll
+      for (int j = 0; j < 16; ++j)
+        if (k0 + j < k_in) dst[j] = (uint16_t)h[j];
+    }
+  }
+}
+
+// Outliers into their slots as bf16(15 v) (15 v is exact in fp32; one rounding to bf16).
+__global__ void scatter_x15_kernel(const int32_t* __restrict__ bidx, const int32_t* __restrict__ off,
+                                   const uint16_t* __restrict__ val, int64_t count, int64_t kpad,
+                                   int64_t n_out, int64_t k_in, uint16_t* __restrict__ out, int64_t ldo) {
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < count;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t g = (int64_t)bidx[i] * kBlock + off[i];
+    const int64_t r = g % kpad, c = g / kpad;
+    if (r < k_in && c < n_out) {
+      const float v15 = 15.0f * __half2float(__ushort_as_half(val[i]));
+      out[c * ldo + r] = __bfloat16_as_ushort(__float2bfloat16_rn(v15));
+    }
+  }
+}
+
+constexpr size_t kLtWorkspace = 32u << 20;
+
+static size_t expand_matrix_bytes(int64_t n_out, int64_t kpad) {
+  return ((size_t)n_out * (size_t)kpad * 2 + 255) & ~(size_t)255;
+}
+
+static int lt_check(cublasStatus_t s, const char* what) {
+  if (s == CUBLAS_STATUS_SUCCESS) return FBFP_OK;
+  return set_error(FBFP_ERR_CUDA, "%s failed (cublas status %d)", what, (int)s);
+}
+
+static cublasLtHandle_t lt_handle(int dev) {
+  static cublasLtHandle_t h[64] = {};
+  if (dev < 0 || dev >= 64) return nullptr;
+  if (!h[dev] && cublasLtCreate(&h[dev]) != CUBLAS_STATUS_SUCCESS) h[dev] = nullptr;
+  return h[dev];
+}
+
+// Y[m, n_out] (bf16 or fp32, row stride ldy) = (X[m, k_in] (bf16, ldx) W15[n_out, k_in]^T
+// (ldw)) / 15 (+ bias, of Y's type). Column-major view for cuBLASLt: D (n_out x m, ld ldy) =
+// alpha op(A) B with A = W15 (k_in x n_out, ld ldw, transposed) and B = X (k_in x m, ld ldx).
+static int lt_gemm_x15(const void* x, int64_t m, int64_t ldx, const void* w15, int64_t ldw,
+                       int64_t n_out, int64_t k_in, const void* bias, void* y, int y_dtype, int64_t ldy,
+                       void* workspace, cudaStream_t st, int dev) {
+  cublasLtHandle_t h = lt_handle(dev);
+  if (!h) return set_error(FBFP_ERR_CUDA, "cublasLtCreate failed");
+  cublasLtMatmulDesc_t op = nullptr;
+  cublasLtMatrixLayout_t la = nullptr, lb = nullptr, lc = nullptr;
+  cublasLtMatmulPreference_t pref = nullptr;
+  int rc = FBFP_OK;
+  const cublasOperation_t ta = CUBLAS_OP_T, tb = CUBLAS_OP_N;
+  const float alpha = 1.0f / 15.0f, beta = 0.0f;
+  const cudaDataType_t yt = y_dtype == FBFP_F32 ? CUDA_R_32F : CUDA_R_16BF;
+  size_t wsb = kLtWorkspace;
+  cublasLtMatmulHeuristicResult_t res = {};
+  int found = 0;
+  do {
+    if ((rc = lt_check(cublasLtMatmulDescCreate(&op, CUBLAS_COMPUTE_32F, CUDA_R_32F), "MatmulDescCreate"))) break;
+    if ((rc = lt_check(cublasLtMatmulDescSetAttribute(op, CUBLASLT_MATMUL_DESC_TRANSA, &ta, sizeof(ta)), "TRANSA"))) break;
+    if ((rc = lt_check(cublasLtMatmulDescSetAttribute(op, CUBLASLT_MATMUL_DESC_TRANSB, &tb, sizeof(tb)), "TRANSB"))) break;
+    if (bias) {
+      const cublasLtEpilogue_t epi = CUBLASLT_EPILOGUE_BIAS;
+      const cudaDataType_t bt = yt;
+      if ((rc = lt_check(cublasLtMatmulDescSetAttribute(op, CUBLASLT_MATMUL_DESC_EPILOGUE, &epi, sizeof(epi)), "EPILOGUE"))) break;
+      if ((rc = lt_check(cublasLtMatmulDescSetAttribute(op, CUBLASLT_MATMUL_DESC_BIAS_POINTER, &bias, sizeof(bias)), "BIAS_POINTER"))) break;
+      if ((rc = lt_check(cublasLtMatmulDescSetAttribute(op, CUBLASLT_MATMUL_DESC_BIAS_DATA_TYPE, &bt, sizeof(bt)), "BIAS_DATA_TYPE"))) break;
+    }
+    if ((rc = lt_check(cublasLtMatrixLayoutCreate(&la, CUDA_R_16BF, (uint64_t)k_in, (uint64_t)n_out, ldw), "layout A"))) break;
+    if ((rc = lt_check(cublasLtMatrixLayoutCreate(&lb, CUDA_R_16BF, (uint64_t)k_in, (uint64_t)m, ldx), "layout B"))) break;
+    if ((rc = lt_check(cublasLtMatrixLayoutCreate(&lc, yt, (uint64_t)n_out, (uint64_t)m, ldy), "layout D"))) break;
+    if ((rc = lt_check(cublasLtMatmulPreferenceCreate(&pref), "PreferenceCreate"))) break;
+    if ((rc = lt_check(cublasLtMatmulPreferenceSetAttribute(pref, CUBLASLT_MATMUL_PREF_MAX_WORKSPACE_BYTES, &wsb, sizeof(wsb)), "PREF_MAX_WORKSPACE"))) break;
+    if ((rc = lt_check(cublasLtMatmulAlgoGetHeuristic(h, op, la, lb, lc, lc, pref, 1, &res, &found), "AlgoGetHeuristic"))) break;
+    if (found < 1) { rc = set_error(FBFP_ERR_CUDA, "cuBLASLt found no algorithm for %lld x %lld x %lld",
+                                    (long long)m, (long long)n_out, (long long)k_in); break; }
+    rc = lt_check(cublasLtMatmul(h, op, &alpha, w15, la, x, lb, &beta, y, lc, y, lc, &res.algo, workspace,
+                                 wsb, st), "cublasLtMatmul");
+  } while (0);
+  if (pref) cublasLtMatmulPreferenceDestroy(pref);
+  if (lc) cublasLtMatrixLayoutDestroy(lc);
+  if (lb) cublasLtMatrixLayoutDestroy(lb);
+  if (la) cublasLtMatrixLayoutDestroy(la);
+  if (op) cublasLtMatmulDescDestroy(op);
+  return rc;
+}
+
+static int grid_blocks(int64_t work, int threads) {
+  int64_t b = (work + threads - 1) / threads;
+  if (b > 148 * 32) b = 148 * 32;
+  return (int)(b < 1 ? 1 : b);
+}
+
+}  // namespace fbfp
+
+using namespace fbfp;
+
+extern "C" int64_t fbfp_gemm_expanded_scratch_bytes(int64_t n_out, int64_t kpad) {
+  if (n_out <= 0 || kpad <= 0) return -1;
+  return (int64_t)(expand_matrix_bytes(n_out, kpad) + kLtWorkspace);
+}
+
+extern "C" int fbfp_expand_x15(const int8_t* exponents, const int16_t* signs, const int32_t* payload,
+                               int64_t n_out, int64_t k_in, int64_t kpad, const int32_t* block_idx,
+                               const int32_t* offset, const uint16_t* value_f16, int64_t count,
+                               void* out, int64_t ldo, void* stream) {
+  FBFP_CHECK_ARG(exponents && signs && payload && out, "null pointer");
+  FBFP_CHECK_ARG(n_out > 0 && k_in > 0 && kpad >= k_in && kpad % kBlock == 0 && ldo >= k_in && ldo % 8 == 0,
+                 "bad shape n_out=%lld k_in=%lld kpad=%lld ldo=%lld", (long long)n_out, (long long)k_in,
+                 (long long)kpad, (long long)ldo);
+  FBFP_CHECK_ARG(((uintptr_t)payload & 7) == 0 && ((uintptr_t)out & 15) == 0,
+                 "payload must be 8-byte and out 16-byte aligned");
+  FBFP_CHECK_ARG(count >= 0 && (count == 0 || (block_idx && offset && value_f16)), "bad outlier list");
+  cudaStream_t st = as_stream(stream);
+  const int64_t kb_row = kpad / kBlock, kb_used = (k_in + kBlock - 1) / kBlock;
+  uint16_t* o = static_cast<uint16_t*>(out);
+  expand_x15_kernel<<<grid_blocks(n_out * kb_used, 256), 256, 0, st>>>(
+      exponents, signs, reinterpret_cast<const uint2*>(payload), n_out, k_in, kb_row, kb_used, o, ldo);
+  FBFP_LAUNCH_CHECK("expand_x15_kernel");
+  if (count > 0) {
+    scatter_x15_kernel<<<grid_blocks(count, 256), 256, 0, st>>>(block_idx, offset, value_f16, count, kpad,
+                                                                n_out, k_in, o, ldo);
+    FBFP_LAUNCH_CHECK("scatter_x15_kernel");
+  }
+  return FBFP_OK;
+}
+
+extern "C" int fbfp_gemm_expanded(const void* x, int64_t m, int64_t ldx, const int8_t* exponents,
+                                  const int16_t* signs, const int32_t* payload, int64_t n_out, int64_t k_in,
+                                  int64_t kpad, const int32_t* block_idx, const int32_t* offset,
+                                  const uint16_t* value_f16, int64_t count, const void* bias, void* y,
+                                  int y_dtype, int64_t ldy, void* scratch, int64_t scratch_bytes,
+                                  void* stream) {
+  FBFP_CHECK_ARG(x && y && scratch, "null pointer");
+  FBFP_CHECK_ARG(y_dtype == FBFP_BF16 || y_dtype == FBFP_F32, "y_dtype must be bf16 or f32");
+  const int64_t ysz = y_dtype == FBFP_F32 ? 4 : 2;
+  FBFP_CHECK_ARG(m > 0 && ldx >= k_in && ldy >= n_out && ldx % 8 == 0 && (ldy * ysz) % 16 == 0,
+                 "bad shape m=%lld ldx=%lld ldy=%lld", (long long)m, (long long)ldx, (long long)ldy);
+  FBFP_CHECK_ARG(((uintptr_t)x & 15) == 0 && ((uintptr_t)y & 15) == 0 && ((uintptr_t)scratch & 255) == 0 &&
+                 (!bias || ((uintptr_t)bias & 15) == 0),
+                 "x, y and bias must be 16-byte and scratch 256-byte aligned");
+  FBFP_CHECK_ARG(kpad > 0 && scratch_bytes >= fbfp_gemm_expanded_scratch_bytes(n_out, kpad),
+                 "scratch of %lld bytes is smaller than fbfp_gemm_expanded_scratch_bytes (%lld)",
+                 (long long)scratch_bytes, (long long)fbfp_gemm_expanded_scratch_bytes(n_out, kpad));
+  int rc = fbfp_expand_x15(exponents, signs, payload, n_out, k_in, kpad, block_idx, offset, value_f16, count,
+                           scratch, kpad, stream);
+  if (rc != FBFP_OK) return rc;
+  int dev = 0;
+  FBFP_CUDA_TRY(cudaGetDevice(&dev));
+  uint8_t* lt_ws = static_cast<uint8_t*>(scratch) + expand_matrix_bytes(n_out, kpad);
+  return lt_gemm_x15(x, m, ldx, scratch, kpad, n_out, k_in, bias, y, y_dtype, ldy, lt_ws, as_stream(stream),
+                     dev);
+}

@@ -91,10 +91,73 @@ def prefill_eligible(X: torch.Tensor, pw: PackedWeight) -> bool:
             and X.stride(0) % 8 == 0 and a16(X) and a16(pw.payload) and a16(pw.signs) and a16(pw.exps))
 
 
+# From this many tokens on, bf16 prefill runs in two passes (fbfp_gemm_expanded): the matrix is
+# expanded once into a bf16 scratch and multiplied by a cuBLASLt GEMM. Below it the fused
+# tcgen05 kernel (fbfp_gemm_prefill) is the faster one, unless it has fewer tiles (128 rows x 256
+# tokens) than the GPU has SMs, which the two-pass path also takes from 256 tokens on.
+EXPANDED_MIN_M = 512
+EXPANDED_MIN_M_FEW_TILES = 256
+_EXPAND_SCRATCH: Dict[int, torch.Tensor] = {}
+_SM_COUNT: Dict[int, int] = {}
+
+
+def expanded_preferred(M: int, pw: PackedWeight, device) -> bool:
+    """Whether packed_linear sends M tokens to the two-pass path (when eligible)."""
+    idx = torch.device(device).index or 0
+    if idx not in _SM_COUNT:
+        _SM_COUNT[idx] = torch.cuda.get_device_properties(idx).multi_processor_count
+    tiles = -(-pw.npad // 128) * -(-M // 256)
+    return M >= EXPANDED_MIN_M or (M >= EXPANDED_MIN_M_FEW_TILES and tiles < _SM_COUNT[idx])
+
+
+def expanded_eligible(X: torch.Tensor, pw: PackedWeight, bias: torch.Tensor | None,
+                      Y: torch.Tensor) -> bool:
+    """Whether fbfp_gemm_expanded takes this call: bf16 activations, a bf16 or fp32 output with a
+    bias (if any) of the same type, 16-byte aligned rows, and not inside a CUDA-graph capture
+    (the scratch may have to grow)."""
+    def ok(t):
+        return (t.stride(-1) == 1 and (t.stride(0) * t.element_size()) % 16 == 0
+                and t.data_ptr() % 16 == 0)
+    return (X.dtype == torch.bfloat16 and Y.dtype in (torch.bfloat16, torch.float32) and ok(X) and ok(Y)
+            and (bias is None or (bias.dtype == Y.dtype and bias.is_contiguous()
+                                  and bias.data_ptr() % 16 == 0))
+            and pw.k_in % 8 == 0 and not torch.cuda.is_current_stream_capturing())
+
+
+def expand_scratch(device: torch.device, nbytes: int) -> torch.Tensor:
+    """The device's scratch for fbfp_gemm_expanded (kept and grown to the largest request)."""
+    idx = torch.device(device).index
+    buf = _EXPAND_SCRATCH.get(idx)
+    if buf is None or buf.numel() < nbytes:
+        _EXPAND_SCRATCH.pop(idx, None)
+        buf = torch.empty(nbytes, dtype=torch.uint8, device=device)
+        _EXPAND_SCRATCH[idx] = buf
+    return buf
+
+
+def gemm_expanded(X: torch.Tensor, pw: PackedWeight, Y: torch.Tensor, bias: torch.Tensor | None = None,
+                  with_outliers: bool = True) -> None:
+    """Y = X @ W^T (+ outliers) (+ bias) in two passes (fbfp_gemm_expanded): the packed matrix
+    expanded into a bf16 scratch as 15 x its values, then a cuBLASLt bf16 GEMM scaled by 1/15."""
+    L = _lib.lib()
+    need = L.fbfp_gemm_expanded_scratch_bytes(pw.n_out, pw.kpad)
+    scratch = expand_scratch(X.device, need)
+    coo = pw.coo if (with_outliers and pw.nnz > 0) else None
+    b, o, v = coo if coo is not None else (None, None, None)
+    _lib.check(L.fbfp_gemm_expanded(_lib.ptr(X), X.shape[0], X.stride(0), _lib.ptr(pw.exps), _lib.ptr(pw.signs),
+                                    _lib.ptr(pw.payload), pw.n_out, pw.k_in, pw.kpad, _lib.ptr(b), _lib.ptr(o),
+                                    _lib.ptr(v), pw.nnz if coo is not None else 0, _lib.ptr(bias), _lib.ptr(Y),
+                                    _lib.dtype_code(Y.dtype, "Y"), Y.stride(0), _lib.ptr(scratch), scratch.numel(),
+                                    _lib.stream_ptr(X.device)), "fbfp_gemm_expanded")
+
+
 def packed_linear(X: torch.Tensor, pw: PackedWeight, bias: torch.Tensor | None = None,
                   out_dtype: torch.dtype | None = None, with_outliers: bool = True,
-                  out: torch.Tensor | None = None) -> torch.Tensor:
-    """Y[M, n_out] = X[M, k] @ W^T (+ outliers) (+ bias) through the CUDA kernels."""
+                  out: torch.Tensor | None = None, prefill: str | None = None) -> torch.Tensor:
+    """Y[M, n_out] = X[M, k] @ W^T (+ outliers) (+ bias) through the CUDA kernels.
+
+    ``prefill`` picks the path for M > 16: "fused" (fbfp_gemm_prefill), "expanded"
+    (fbfp_gemm_expanded, where eligible) or None (``expanded_preferred``)."""
     L = _lib.lib()
     _lib.require_cuda(X, "X")
     if X.dim() != 2:
@@ -116,6 +179,10 @@ def packed_linear(X: torch.Tensor, pw: PackedWeight, bias: torch.Tensor | None =
     bd = _lib.dtype_code(bias.dtype, "bias") if bias is not None else 0
     ws = gemv_workspace(X.device, pw.npad)
     st = _lib.stream_ptr(X.device)
+    if M > 16 and prefill != "fused" and (prefill == "expanded" or expanded_preferred(M, pw, X.device)) \
+            and expanded_eligible(X, pw, bias, Y):
+        gemm_expanded(X, pw, Y, bias, with_outliers)
+        return Y
     if M > 16 and prefill_eligible(X, pw):
         _lib.check(L.fbfp_gemm_prefill(_lib.ptr(X), xd, M, X.stride(0), _lib.ptr(pw.exps),
                                        _lib.ptr(pw.signs), _lib.ptr(pw.payload), pw.n_out, pw.k_in,

@@ -215,6 +215,35 @@ int fbfp_gemm_prefill(const void* x, int x_dtype, int64_t m, int64_t ldx,
                       void* workspace, void* stream);
 
 /* ------------------------------------------------------------------------------------
+ * Two-pass prefill for many tokens (bf16 in; bf16 or fp32 out): the packed matrix is expanded into a bf16
+ * scratch holding 15 x its dequantised values, then a cuBLASLt bf16 GEMM (fp32 accumulation,
+ * alpha = 1/15, bias in its epilogue) gives
+ *   y[m, n] = sum_k x[m, k] * W_full[n, k] + bias[n]
+ * as fbfp_gemm_prefill does, with the same bf16 operand: dense elements s * m * 2^e exactly and
+ * outliers bf16(15 v) (the reference's oabf_gemm, triton_kernel.py:130-195, rounds the
+ * dequantised weight s * fl(m / 15) * 2^e to the activation dtype instead). The outliers come
+ * as the COO list of the compressor (block_idx, offset, fp16 value bits; count may be 0).
+ * Requirements: x bf16, y and bias (optional) both bf16 or both fp32 (y_dtype), all 16-byte
+ * aligned with 16-byte row strides (ldx a multiple of 8); scratch
+ * 256-byte aligned, at least fbfp_gemm_expanded_scratch_bytes(n_out, kpad) bytes (the expanded
+ * matrix, n_out x kpad bf16, then the GEMM's workspace). No counterpart in the reference.
+ * ---------------------------------------------------------------------------------- */
+int64_t fbfp_gemm_expanded_scratch_bytes(int64_t n_out, int64_t kpad);
+int fbfp_gemm_expanded(const void* x, int64_t m, int64_t ldx, const int8_t* exponents,
+                       const int16_t* signs, const int32_t* payload, int64_t n_out, int64_t k_in,
+                       int64_t kpad, const int32_t* block_idx, const int32_t* offset,
+                       const uint16_t* value_f16, int64_t count, const void* bias, void* y,
+                       int y_dtype, int64_t ldy, void* scratch, int64_t scratch_bytes, void* stream);
+
+/* The expansion alone: out[n * ldo + k] = bf16 of 15 x the dequantised W_full[n, k] for
+ * n < n_out, k < k_in (dense s * m * 2^e exactly, outliers bf16(15 v)); ldo a multiple of 8,
+ * out 16-byte aligned. */
+int fbfp_expand_x15(const int8_t* exponents, const int16_t* signs, const int32_t* payload,
+                    int64_t n_out, int64_t k_in, int64_t kpad, const int32_t* block_idx,
+                    const int32_t* offset, const uint16_t* value_f16, int64_t count,
+                    void* out, int64_t ldo, void* stream);
+
+/* ------------------------------------------------------------------------------------
  * Tensor-parallel exchange: one-shot fp32 sum all-reduce over NVLink peer memory (plain peer
  * stores and loads, bounded waits). Replaces the collective of the row-parallel linears (the
  * reference has no multi-GPU path; this is the exchange of the sharded o/down projections).
