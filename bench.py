@@ -79,16 +79,23 @@ class Clocks:
         self.index = index
         self.proc = None
         self.lines = []
+        self.n0 = 0
 
     def __enter__(self):
+        # the sampler is running (its first sample read) before the timed region starts, and only
+        # samples read after that count: a short region (a few steps on many GPUs) still gets some
         try:
             self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.Q}", "--format=csv,noheader,nounits",
-                                          "-i", str(self.index), "-lms", "100"],
+                                          "-i", str(self.index), "-lms", "20"],
                                          stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
             self.t = threading.Thread(target=self._read, daemon=True)
             self.t.start()
+            t_end = time.monotonic() + 5.0
+            while not self.lines and time.monotonic() < t_end and self.proc.poll() is None:
+                time.sleep(0.005)
         except Exception:
             self.proc = None
+        self.n0 = len(self.lines)
         return self
 
     def _read(self):
@@ -97,6 +104,10 @@ class Clocks:
 
     def __exit__(self, *exc):
         if self.proc is not None:
+            # at least one sample read after the region began (taken during it or as it ends)
+            t_end = time.monotonic() + 0.5
+            while len(self.lines) <= self.n0 and time.monotonic() < t_end and self.proc.poll() is None:
+                time.sleep(0.005)
             self.proc.terminate()
             try:
                 self.proc.wait(timeout=5)
@@ -106,7 +117,7 @@ class Clocks:
     def summary(self):
         sm, mx, reasons = [], None, set()
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for ln in self.lines:
+        for ln in self.lines[self.n0:]:
             f = [x.strip() for x in ln.split(",")]
             if len(f) < 9:
                 continue
