@@ -569,7 +569,7 @@ def run_prefill(layers, device, ms=(512, 2048, 8192), iters=5):
     at M bf16 tokens through packed_linear, on both paths: the fused tcgen05 kernel
     (fbfp_gemm_prefill) and the two-pass one (fbfp_gemm_expanded: expansion of the packed matrix
     into a bf16 scratch, then a cuBLASLt bf16 GEMM), which packed_linear takes where
-    ``expanded_preferred`` says so (512 tokens, or 256 when the fused kernel would have fewer tiles
+    ``expanded_preferred`` says so (512 tokens, or 32 when the fused kernel would have fewer tiles
     than SMs); beside cuBLAS bf16 on a dense bf16 weight of the same shape. CUDA events on the
     launching stream; 3 warm-up launches."""
     from flashbfp_b200 import workloads

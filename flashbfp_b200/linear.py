@@ -94,9 +94,11 @@ def prefill_eligible(X: torch.Tensor, pw: PackedWeight) -> bool:
 # From this many tokens on, bf16 prefill runs in two passes (fbfp_gemm_expanded): the matrix is
 # expanded once into a bf16 scratch and multiplied by a cuBLASLt GEMM. Below it the fused
 # tcgen05 kernel (fbfp_gemm_prefill) is the faster one, unless it has fewer tiles (128 rows x 256
-# tokens) than the GPU has SMs, which the two-pass path also takes from 256 tokens on.
+# tokens) than the GPU has SMs, which the two-pass path also takes from 32 tokens on (measured:
+# a 3840x15360 matrix at 128 tokens 83 against 182 us, 8192x3840 45 against 60 us; a
+# 30720x3840 one, 240 fused tiles, keeps the fused kernel: 111 against 154 us).
 EXPANDED_MIN_M = 512
-EXPANDED_MIN_M_FEW_TILES = 256
+EXPANDED_MIN_M_FEW_TILES = 32
 _EXPAND_SCRATCH: Dict[int, torch.Tensor] = {}
 _SM_COUNT: Dict[int, int] = {}
 
