@@ -14,44 +14,66 @@
 
 namespace fbfp {
 
+// The 16 bf16 values s * m * 2^e of one block as 8 pair words (element 2j in the low half).
+// For e in [-120, 120]: a pair of nibbles placed under the biased exponent E = e + 134 reads as
+// 2^e (128 + m) per element, and a paired bf16 subtraction of 2^e * 128 leaves m * 2^e exactly
+// (a normal number, or zero); the signs are then xor-ed into bits 15 and 31. Other exponents take
+// the fp32 product m * 2^e (exact, zero low half) element by element.
+__device__ __forceinline__ void expand_pairs(uint2 w, uint32_t s, int e, uint32_t (&o)[8]) {
+  // sign bit 2j at bit 2j and sign bit 2j + 1 at bit 2j + 16, so (sp << (15 - 2j)) puts pair j's
+  // two signs at bits 15 and 31
+  const uint32_t sp = (s & 0x5555u) | ((s & 0xAAAAu) << 15);
+  if (e >= -120 && e <= 120) {
+    const uint32_t K = (uint32_t)(e + 134) * 0x00800080u;
+    const __nv_bfloat162 kb = *reinterpret_cast<const __nv_bfloat162*>(&K);
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      const uint32_t word = h ? w.y : w.x;
+      const uint32_t lo = word & 0x0F0F0F0Fu, hi = (word >> 4) & 0x0F0F0F0Fu;   // elements 2j', 2j'+1
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const int j = 4 * h + q;
+        const uint32_t pr = (__byte_perm(lo, hi, (uint32_t)(q | (q << 4) | ((4 + q) << 8) | ((4 + q) << 12))) &
+                             0x000F000Fu) | K;
+        __nv_bfloat162 d = __hsub2(*reinterpret_cast<const __nv_bfloat162*>(&pr), kb);
+        o[j] = *reinterpret_cast<uint32_t*>(&d) ^ ((sp << (15 - 2 * j)) & 0x80008000u);
+      }
+    }
+  } else {
+    const float scale = __uint_as_float((uint32_t)(e + 127 < 0 ? 0 : e + 127) << 23);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const uint32_t word = j < 4 ? w.x : w.y;
+      const uint32_t m0 = (word >> (8 * (j & 3))) & 0xFu, m1 = (word >> (8 * (j & 3) + 4)) & 0xFu;
+      const uint32_t f0 = __float_as_uint((float)m0 * scale) >> 16, f1 = __float_as_uint((float)m1 * scale) >> 16;
+      o[j] = (f0 | (f1 << 16)) ^ ((sp << (15 - 2 * j)) & 0x80008000u);
+    }
+  }
+}
+
 // One thread per 16-weight block: 11 packed bytes in, 32 bytes out (two 16-byte stores when the
-// block lies inside k_in, else element by element).
+// block lies inside k_in, else element by element). Rows stride over grid y, a row's blocks over
+// grid x (no index division).
 __global__ void expand_x15_kernel(const int8_t* __restrict__ ex, const int16_t* __restrict__ sg,
                                   const uint2* __restrict__ pay, int64_t n_out, int64_t k_in,
                                   int64_t kb_row, int64_t kb_used, uint16_t* __restrict__ out,
                                   int64_t ldo) {
-  const int64_t total = n_out * kb_used;
-  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total;
-       i += (int64_t)gridDim.x * blockDim.x) {
-    const int64_t n = i / kb_used, kb = i - n * kb_used;
-    const int64_t b = n * kb_row + kb;
-    const uint2 w = pay[b];
-    const uint32_t s = (uint16_t)sg[b];
-    const uint32_t ebits = (uint32_t)((int)ex[b] + 127) << 23;        // 2^e as fp32 bits
-    const float scale = __uint_as_float(ebits);
-    uint32_t h[16];
+  for (int64_t n = blockIdx.y; n < n_out; n += gridDim.y) {
+    for (int64_t kb = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; kb < kb_used;
+         kb += (int64_t)gridDim.x * blockDim.x) {
+      const int64_t b = n * kb_row + kb;
+      uint32_t o[8];
+      expand_pairs(pay[b], (uint16_t)sg[b], (int)ex[b], o);
+      const int64_t k0 = kb * kBlock;
+      uint16_t* dst = out + n * ldo + k0;
+      if (k0 + kBlock <= k_in) {
+        reinterpret_cast<uint4*>(dst)[0] = make_uint4(o[0], o[1], o[2], o[3]);
+        reinterpret_cast<uint4*>(dst)[1] = make_uint4(o[4], o[5], o[6], o[7]);
+      } else {
 #pragma unroll
-    for (int j = 0; j < 16; ++j) {
-      const uint32_t word = j < 8 ? w.x : w.y;
-      const uint32_t m = (word >> (4 * (j & 7))) & 0xFu;
-      // m * 2^e is exact in fp32 with zero low 16 bits, so its top half is the bf16 value
-      const uint32_t f = __float_as_uint((float)m * scale) | (((s >> j) & 1u) << 31);
-      h[j] = f >> 16;
-    }
-    const int64_t k0 = kb * kBlock;
-    uint16_t* dst = out + n * ldo + k0;
-    if (k0 + kBlock <= k_in) {
-      uint4 v0, v1;
-      v0.x = h[0] | (h[1] << 16);  v0.y = h[2] | (h[3] << 16);
-      v0.z = h[4] | (h[5] << 16);  v0.w = h[6] | (h[7] << 16);
-      v1.x = h[8] | (h[9] << 16);  v1.y = h[10] | (h[11] << 16);
-      v1.z = h[12] | (h[13] << 16); v1.w = h[14] | (h[15] << 16);
-      reinterpret_cast<uint4*>(dst)[0] = v0;
-      reinterpret_cast<uint4*>(dst)[1] = v1;
-    } else {
-#pragma unroll
-      for (int j = 0; j < 16; ++j)
-        if (k0 + j < k_in) dst[j] = (uint16_t)h[j];
+        for (int j = 0; j < 16; ++j)
+          if (k0 + j < k_in) dst[j] = (uint16_t)(o[j >> 1] >> (16 * (j & 1)));
+      }
     }
   }
 }
@@ -166,7 +188,10 @@ extern "C" int fbfp_expand_x15(const int8_t* exponents, const int16_t* signs, co
   cudaStream_t st = as_stream(stream);
   const int64_t kb_row = kpad / kBlock, kb_used = (k_in + kBlock - 1) / kBlock;
   uint16_t* o = static_cast<uint16_t*>(out);
-  expand_x15_kernel<<<grid_blocks(n_out * kb_used, 256), 256, 0, st>>>(
+  const int threads = 128;
+  const int64_t gx = (kb_used + threads - 1) / threads;
+  const int64_t gy = n_out < 32768 ? n_out : 32768;
+  expand_x15_kernel<<<dim3((unsigned)gx, (unsigned)gy), threads, 0, st>>>(
       exponents, signs, reinterpret_cast<const uint2*>(payload), n_out, k_in, kb_row, kb_used, o, ldo);
   FBFP_LAUNCH_CHECK("expand_x15_kernel");
   if (count > 0) {
