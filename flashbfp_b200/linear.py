@@ -433,3 +433,45 @@ class OABFLinear(torch.nn.Module):
             sp = {"block_idx": z, "offset": z.clone(),
                   "value": torch.zeros(0, dtype=torch.float16, device=device), "count": 0}
         self.load_compressed(dp, sp, device)
+
+
+def _main(argv=None) -> None:
+    """``python -m flashbfp_b200.linear [N K M [path [reps]]]``: time ``packed_linear`` on a seeded
+    N x K OABF weight (N(0, 0.02) bf16 with 1.5% heavy-tailed outliers, compressed on the GPU) at M
+    bf16 tokens, after two warm-up calls; ``path`` is fused, expanded or auto (the default
+    choice). Prints the time per call and the tensor rate."""
+    import json
+    import sys
+    from . import workloads
+    from .compressor import OABFCompressor
+    args = sys.argv[1:] if argv is None else list(argv)
+    n, k, m = (int(args[0]), int(args[1]), int(args[2])) if len(args) >= 3 else (30720, 3840, 2048)
+    path = args[3] if len(args) >= 4 else "auto"
+    reps = int(args[4]) if len(args) >= 5 else 5
+    if path not in ("fused", "expanded", "auto"):
+        raise SystemExit("path must be fused, expanded or auto")
+    dev = torch.device("cuda", torch.cuda.current_device())
+    W = workloads.decode_weight(n, k, seed=21, device=dev)
+    dp, sp = OABFCompressor().compress_matrix_device(W)
+    del W
+    pw = from_compressed(dp, sp, dev)
+    X = workloads.activations(m, k, seed=11, device=dev)
+    Y = torch.empty(m, n, dtype=torch.bfloat16, device=dev)
+    choice = None if path == "auto" else path
+    for _ in range(2):
+        packed_linear(X, pw, out=Y, prefill=choice)
+    torch.cuda.synchronize(dev)
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    for _ in range(reps):
+        packed_linear(X, pw, out=Y, prefill=choice)
+    b.record()
+    torch.cuda.synchronize(dev)
+    check_device_errors(dev)
+    ms = a.elapsed_time(b) / reps
+    print(json.dumps({"shape": [n, k], "m": m, "path": path, "ms": round(ms, 4),
+                      "tflops": round(2.0 * m * n * k / ms / 1e9, 1)}))
+
+
+if __name__ == "__main__":
+    _main()
