@@ -75,9 +75,10 @@ _PROTOS = {
                                    _c_i64, _vp, _vp, _vp, _c_int, _vp, _c_int, _c_i64, _vp, _vp]),
     "fbfp_gemm_expanded_scratch_bytes": (_c_i64, [_c_i64, _c_i64]),
     "fbfp_gemm_expanded": (_c_int, [_vp, _c_i64, _c_i64, _vp, _vp, _vp, _c_i64, _c_i64, _c_i64, _vp, _vp,
-                                    _vp, _c_i64, _vp, _vp, _c_int, _c_i64, _vp, _c_i64, _vp]),
-    "fbfp_expand_x15": (_c_int, [_vp, _vp, _vp, _c_i64, _c_i64, _c_i64, _vp, _vp, _vp, _c_i64, _vp,
-                                 _c_i64, _vp]),
+                                    _vp, _c_i64, _vp, _vp, _c_i64, _vp, _vp, _c_int, _c_i64, _vp, _c_i64,
+                                    _vp]),
+    "fbfp_expand_x15": (_c_int, [_vp, _vp, _vp, _c_i64, _c_i64, _c_i64, _vp, _vp, _vp, _c_i64, _vp, _vp,
+                                 _c_i64, _vp, _c_i64, _vp]),
     "fbfp_compress_scratch_bytes": (_c_i64, [_c_i64, _c_i64, _c_i64, _c_i64]),
     "fbfp_compress_threshold": (_c_int, [_vp, _c_int, _c_i64, _c_i64, _c_i64, _vp, _vp, _vp]),
     "fbfp_compress_pack": (_c_int, [_vp, _c_int, _c_i64, _c_i64, _c_i64, _c_i64, _c_i64, _vp, _vp,

@@ -51,19 +51,51 @@ __device__ __forceinline__ void expand_pairs(uint2 w, uint32_t s, int e, uint32_
   }
 }
 
+// Tile-grouped outlier index (outliers.cu): entries by (128-row group, 256-column stage) segment,
+// seg_ptr[0 .. nseg] the segment starts, then per segment 136 uint16 row starts.
+struct TileIndex {
+  const uint32_t* entries;   // null: no index (outliers come from the COO list)
+  const int32_t* seg_ptr;
+  int64_t n_stages, roff_base;
+};
+
+// Outliers of row n inside block kb: bf16(15 v) into their (+0) slots of the block's pairs.
+__device__ __forceinline__ void patch_block(const TileIndex& t, int64_t n, int64_t kb, uint32_t (&o)[8]) {
+  const int64_t sgm = (n >> 7) * t.n_stages + (kb >> 4);
+  const int lr = (int)(n & 127);
+  const uint16_t* ro = reinterpret_cast<const uint16_t*>(t.seg_ptr + t.roff_base) + sgm * 136;
+  const int k0 = __ldg(ro + lr), k1 = __ldg(ro + lr + 1);
+  if (k0 == k1) return;
+  const uint32_t* es = t.entries + __ldg(t.seg_ptr + sgm);
+  const int want = (int)(kb & 15);
+  for (int k = k0; k < k1; ++k) {            // the row's entries of this stage, by column
+    const uint32_t e = __ldg(es + k);
+    const int c = (int)((e >> 16) & 0xFFu);
+    if ((c >> 4) != want) continue;
+    const float v15 = 15.0f * __half2float(__ushort_as_half((unsigned short)(e & 0xFFFFu)));
+    const uint32_t bits = __bfloat16_as_ushort(__float2bfloat16_rn(v15));
+    const int el = c & 15;
+    const uint32_t keep = (el & 1) ? 0x0000FFFFu : 0xFFFF0000u, put = (el & 1) ? (bits << 16) : bits;
+#pragma unroll
+    for (int q = 0; q < 8; ++q)
+      if (q == (el >> 1)) o[q] = (o[q] & keep) | put;
+  }
+}
+
 // One thread per 16-weight block: 11 packed bytes in, 32 bytes out (two 16-byte stores when the
-// block lies inside k_in, else element by element). Rows stride over grid y, a row's blocks over
-// grid x (no index division).
+// block lies inside k_in, else element by element), with the block's outliers written in when the
+// tile index is given. Rows stride over grid y, a row's blocks over grid x (no index division).
 __global__ void expand_x15_kernel(const int8_t* __restrict__ ex, const int16_t* __restrict__ sg,
                                   const uint2* __restrict__ pay, int64_t n_out, int64_t k_in,
-                                  int64_t kb_row, int64_t kb_used, uint16_t* __restrict__ out,
-                                  int64_t ldo) {
+                                  int64_t kb_row, int64_t kb_used, TileIndex tix,
+                                  uint16_t* __restrict__ out, int64_t ldo) {
   for (int64_t n = blockIdx.y; n < n_out; n += gridDim.y) {
     for (int64_t kb = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; kb < kb_used;
          kb += (int64_t)gridDim.x * blockDim.x) {
       const int64_t b = n * kb_row + kb;
       uint32_t o[8];
       expand_pairs(pay[b], (uint16_t)sg[b], (int)ex[b], o);
+      if (tix.entries) patch_block(tix, n, kb, o);
       const int64_t k0 = kb * kBlock;
       uint16_t* dst = out + n * ldo + k0;
       if (k0 + kBlock <= k_in) {
@@ -177,6 +209,7 @@ extern "C" int64_t fbfp_gemm_expanded_scratch_bytes(int64_t n_out, int64_t kpad)
 extern "C" int fbfp_expand_x15(const int8_t* exponents, const int16_t* signs, const int32_t* payload,
                                int64_t n_out, int64_t k_in, int64_t kpad, const int32_t* block_idx,
                                const int32_t* offset, const uint16_t* value_f16, int64_t count,
+                               const uint32_t* entries, const int32_t* seg_ptr, int64_t npad,
                                void* out, int64_t ldo, void* stream) {
   FBFP_CHECK_ARG(exponents && signs && payload && out, "null pointer");
   FBFP_CHECK_ARG(n_out > 0 && k_in > 0 && kpad >= k_in && kpad % kBlock == 0 && ldo >= k_in && ldo % 8 == 0,
@@ -184,17 +217,24 @@ extern "C" int fbfp_expand_x15(const int8_t* exponents, const int16_t* signs, co
                  (long long)kpad, (long long)ldo);
   FBFP_CHECK_ARG(((uintptr_t)payload & 7) == 0 && ((uintptr_t)out & 15) == 0,
                  "payload must be 8-byte and out 16-byte aligned");
-  FBFP_CHECK_ARG(count >= 0 && (count == 0 || (block_idx && offset && value_f16)), "bad outlier list");
+  const bool tiles = entries && seg_ptr;
+  FBFP_CHECK_ARG(tiles || count == 0 || (count > 0 && block_idx && offset && value_f16), "bad outlier list");
+  FBFP_CHECK_ARG(!tiles || npad >= n_out, "npad < n_out");
   cudaStream_t st = as_stream(stream);
   const int64_t kb_row = kpad / kBlock, kb_used = (k_in + kBlock - 1) / kBlock;
   uint16_t* o = static_cast<uint16_t*>(out);
+  TileIndex tix = {nullptr, nullptr, 0, 0};
+  if (tiles) {
+    const int64_t n_stages = (kb_row + 15) / 16, nseg = ((npad + 127) / 128) * n_stages;
+    tix = {entries, seg_ptr, n_stages, (nseg + 1 + 3) & ~(int64_t)3};
+  }
   const int threads = 128;
   const int64_t gx = (kb_used + threads - 1) / threads;
   const int64_t gy = n_out < 32768 ? n_out : 32768;
   expand_x15_kernel<<<dim3((unsigned)gx, (unsigned)gy), threads, 0, st>>>(
-      exponents, signs, reinterpret_cast<const uint2*>(payload), n_out, k_in, kb_row, kb_used, o, ldo);
+      exponents, signs, reinterpret_cast<const uint2*>(payload), n_out, k_in, kb_row, kb_used, tix, o, ldo);
   FBFP_LAUNCH_CHECK("expand_x15_kernel");
-  if (count > 0) {
+  if (!tiles && count > 0) {
     scatter_x15_kernel<<<grid_blocks(count, 256), 256, 0, st>>>(block_idx, offset, value_f16, count, kpad,
                                                                 n_out, k_in, o, ldo);
     FBFP_LAUNCH_CHECK("scatter_x15_kernel");
@@ -205,7 +245,8 @@ extern "C" int fbfp_expand_x15(const int8_t* exponents, const int16_t* signs, co
 extern "C" int fbfp_gemm_expanded(const void* x, int64_t m, int64_t ldx, const int8_t* exponents,
                                   const int16_t* signs, const int32_t* payload, int64_t n_out, int64_t k_in,
                                   int64_t kpad, const int32_t* block_idx, const int32_t* offset,
-                                  const uint16_t* value_f16, int64_t count, const void* bias, void* y,
+                                  const uint16_t* value_f16, int64_t count, const uint32_t* entries,
+                                  const int32_t* seg_ptr, int64_t npad, const void* bias, void* y,
                                   int y_dtype, int64_t ldy, void* scratch, int64_t scratch_bytes,
                                   void* stream) {
   FBFP_CHECK_ARG(x && y && scratch, "null pointer");
@@ -220,7 +261,7 @@ extern "C" int fbfp_gemm_expanded(const void* x, int64_t m, int64_t ldx, const i
                  "scratch of %lld bytes is smaller than fbfp_gemm_expanded_scratch_bytes (%lld)",
                  (long long)scratch_bytes, (long long)fbfp_gemm_expanded_scratch_bytes(n_out, kpad));
   int rc = fbfp_expand_x15(exponents, signs, payload, n_out, k_in, kpad, block_idx, offset, value_f16, count,
-                           scratch, kpad, stream);
+                           entries, seg_ptr, npad, scratch, kpad, stream);
   if (rc != FBFP_OK) return rc;
   int dev = 0;
   FBFP_CUDA_TRY(cudaGetDevice(&dev));

@@ -144,11 +144,15 @@ def gemm_expanded(X: torch.Tensor, pw: PackedWeight, Y: torch.Tensor, bias: torc
     L = _lib.lib()
     need = L.fbfp_gemm_expanded_scratch_bytes(pw.n_out, pw.kpad)
     scratch = expand_scratch(X.device, need)
+    # the outliers as the COO list (a separate scatter launch): writing them inside the
+    # expansion from the tile-grouped index measured no faster (one more dependent load chain
+    # per block)
     coo = pw.coo if (with_outliers and pw.nnz > 0) else None
     b, o, v = coo if coo is not None else (None, None, None)
     _lib.check(L.fbfp_gemm_expanded(_lib.ptr(X), X.shape[0], X.stride(0), _lib.ptr(pw.exps), _lib.ptr(pw.signs),
                                     _lib.ptr(pw.payload), pw.n_out, pw.k_in, pw.kpad, _lib.ptr(b), _lib.ptr(o),
-                                    _lib.ptr(v), pw.nnz if coo is not None else 0, _lib.ptr(bias), _lib.ptr(Y),
+                                    _lib.ptr(v), pw.nnz if coo is not None else 0,
+                                    None, None, pw.npad, _lib.ptr(bias), _lib.ptr(Y),
                                     _lib.dtype_code(Y.dtype, "Y"), Y.stride(0), _lib.ptr(scratch), scratch.numel(),
                                     _lib.stream_ptr(X.device)), "fbfp_gemm_expanded")
 

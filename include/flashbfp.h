@@ -222,7 +222,9 @@ int fbfp_gemm_prefill(const void* x, int x_dtype, int64_t m, int64_t ldx,
  * as fbfp_gemm_prefill does, with the same bf16 operand: dense elements s * m * 2^e exactly and
  * outliers bf16(15 v) (the reference's oabf_gemm, triton_kernel.py:130-195, rounds the
  * dequantised weight s * fl(m / 15) * 2^e to the activation dtype instead). The outliers come
- * as the COO list of the compressor (block_idx, offset, fp16 value bits; count may be 0).
+ * as the tile-grouped index of fbfp_outlier_tiles_build (entries, seg_ptr, built for npad rows;
+ * written inside the expansion) or, with entries or seg_ptr null, as the COO list of the
+ * compressor (block_idx, offset, fp16 value bits; count may be 0; a separate scatter).
  * Requirements: x bf16, y and bias (optional) both bf16 or both fp32 (y_dtype), all 16-byte
  * aligned with 16-byte row strides (ldx a multiple of 8); scratch
  * 256-byte aligned, at least fbfp_gemm_expanded_scratch_bytes(n_out, kpad) bytes (the expanded
@@ -232,7 +234,8 @@ int64_t fbfp_gemm_expanded_scratch_bytes(int64_t n_out, int64_t kpad);
 int fbfp_gemm_expanded(const void* x, int64_t m, int64_t ldx, const int8_t* exponents,
                        const int16_t* signs, const int32_t* payload, int64_t n_out, int64_t k_in,
                        int64_t kpad, const int32_t* block_idx, const int32_t* offset,
-                       const uint16_t* value_f16, int64_t count, const void* bias, void* y,
+                       const uint16_t* value_f16, int64_t count, const uint32_t* entries,
+                       const int32_t* seg_ptr, int64_t npad, const void* bias, void* y,
                        int y_dtype, int64_t ldy, void* scratch, int64_t scratch_bytes, void* stream);
 
 /* The expansion alone: out[n * ldo + k] = bf16 of 15 x the dequantised W_full[n, k] for
@@ -241,6 +244,7 @@ int fbfp_gemm_expanded(const void* x, int64_t m, int64_t ldx, const int8_t* expo
 int fbfp_expand_x15(const int8_t* exponents, const int16_t* signs, const int32_t* payload,
                     int64_t n_out, int64_t k_in, int64_t kpad, const int32_t* block_idx,
                     const int32_t* offset, const uint16_t* value_f16, int64_t count,
+                    const uint32_t* entries, const int32_t* seg_ptr, int64_t npad,
                     void* out, int64_t ldo, void* stream);
 
 /* ------------------------------------------------------------------------------------

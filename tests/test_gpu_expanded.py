@@ -79,16 +79,22 @@ def _expected_x15(pw):
     return out
 
 
+@pytest.mark.parametrize("index", ["tiles", "coo"])
 @pytest.mark.parametrize("shape", [(4096, 3840), (192, 256), (200, 520)])
-def test_expansion_bit_exact(shape):
+def test_expansion_bit_exact(shape, index):
+    """Outliers from the tile-grouped index (written inside the expansion) or from the COO list
+    (a separate scatter): the same bits either way."""
     n, k = shape
     pw, _ = _layer(n, k)
+    assert pw.entries is not None and pw.nnz > 0
     L = _lib.lib()
     ldo = (k + 7) // 8 * 8
     out = torch.full((n, ldo), -1, dtype=torch.int16, device="cuda")
-    b, o, v = pw.coo if pw.nnz else (None, None, None)
+    b, o, v = pw.coo if index == "coo" else (None, None, None)
+    ent, seg = (pw.entries, pw.seg_ptr) if index == "tiles" else (None, None)
     _lib.check(L.fbfp_expand_x15(_lib.ptr(pw.exps), _lib.ptr(pw.signs), _lib.ptr(pw.payload), n, k, pw.kpad,
-                                 _lib.ptr(b), _lib.ptr(o), _lib.ptr(v), pw.nnz, _lib.ptr(out), ldo,
+                                 _lib.ptr(b), _lib.ptr(o), _lib.ptr(v), pw.nnz if index == "coo" else 0,
+                                 _lib.ptr(ent), _lib.ptr(seg), pw.npad, _lib.ptr(out), ldo,
                                  _lib.stream_ptr(out.device)), "fbfp_expand_x15")
     exp = _expected_x15(pw).view(torch.int16)
     assert torch.equal(out[:, :k], exp)
@@ -160,7 +166,7 @@ def test_expanded_rejects_small_scratch():
     Y = torch.empty(64, 192, dtype=torch.bfloat16, device="cuda")
     small = torch.empty(4096, dtype=torch.uint8, device="cuda")
     st = L.fbfp_gemm_expanded(_lib.ptr(X), 64, 256, _lib.ptr(pw.exps), _lib.ptr(pw.signs), _lib.ptr(pw.payload),
-                              pw.n_out, pw.k_in, pw.kpad, None, None, None, 0, None, _lib.ptr(Y),
-                              _lib.DTYPE_CODE[torch.bfloat16], 192, _lib.ptr(small), small.numel(),
+                              pw.n_out, pw.k_in, pw.kpad, None, None, None, 0, None, None, pw.npad, None,
+                              _lib.ptr(Y), _lib.DTYPE_CODE[torch.bfloat16], 192, _lib.ptr(small), small.numel(),
                               _lib.stream_ptr(X.device))
     assert st == 1 and b"scratch" in L.fbfp_last_error()
